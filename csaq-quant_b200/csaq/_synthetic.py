@@ -37,15 +37,19 @@ class MixedLinearCase:
 
 
 def tier_split(n_rows: int, fracs=(0.1, 0.2)) -> List[int]:
-    """Row counts per tier for a 16/8/4 split: floor(0.1N), floor(0.2N), rest."""
-    n16 = int(math.floor(fracs[0] * n_rows))
-    n8 = int(math.floor(fracs[1] * n_rows))
-    return [n16, n8, n_rows - n16 - n8]
+    """Row counts per tier: floor(f * N) for each fraction, the rest last
+    (default 16/8/4: floor(0.1N), floor(0.2N), rest)."""
+    counts = [int(math.floor(f * n_rows)) for f in fracs]
+    return counts + [n_rows - sum(counts)]
 
 
 def mixed_linear(n: int = 4096, k: int = 4096, m: int = 1, seed: int = 0,
                  dtype: torch.dtype = torch.float16, outlier_frac: float = 0.01,
-                 bits=(16, 8, 4)) -> MixedLinearCase:
+                 bits=(16, 8, 4), fracs=(0.1, 0.2)) -> MixedLinearCase:
+    """`bits` lists the tiers from most to least salient; `fracs` gives the
+    fraction of rows of every tier but the last."""
+    if len(bits) != len(fracs) + 1 or len(set(bits)) != len(bits):
+        raise ValueError("need len(bits) == len(fracs) + 1 and distinct bit-widths")
     gen = torch.Generator().manual_seed(seed)
     W = torch.randn(n, k, generator=gen) * 0.02
     n_out = max(1, int(outlier_frac * n))
@@ -55,7 +59,7 @@ def mixed_linear(n: int = 4096, k: int = 4096, m: int = 1, seed: int = 0,
     G = (torch.randn(n, k, generator=gen) * 1e-3).to(dtype)
     sal = (G.float() * W.float()).abs().sum(dim=1)
     order = torch.argsort(sal, descending=True, stable=True)
-    counts = tier_split(n)
+    counts = tier_split(n, fracs)
     tier_rows = {}
     start = 0
     for b, c in zip(bits, counts):

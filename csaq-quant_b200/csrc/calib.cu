@@ -1,0 +1,375 @@
+// Calibration kernels: co-activation masks, popcount intersection counts,
+// Jaccard threshold bits, the seed-order clique partition and the salience
+// accumulator.
+//
+// Mask layout ("channel-major bits"): mask[c][w] is a uint32 whose bit b is
+// token 32*w + b of channel c; tokens past the end are 0. With this layout the
+// intersection count of channels i and j is sum_w popc(mask[i][w] & mask[j][w])
+// and the activation count f_i is sum_w popc(mask[i][w]), both exact integers,
+// equal to the fp32 matmul counts of csaq/core.py:261-263.
+
+#include "common.cuh"
+
+namespace csaq {
+namespace {
+
+constexpr int kThreads = 256;
+
+// ── masks ───────────────────────────────────────────────────────────────────
+// One thread per channel, 32 tokens per block row: act[t][c] reads are
+// coalesced across channels; each thread writes one 32-bit word.
+// mode 0: act > thr (compared in fp32; every fp16/bf16 value and thr = 0.5
+//         are exact in fp32, so this is the comparison in the input dtype).
+// mode 1: |act| >= tok_thr[t] (top-k hook of csaq/core.py:143-155), compared
+//         on the magnitude bit patterns, which order like the values.
+template <typename T>
+__global__ void mask_kernel(const T* __restrict__ act, int64_t n_tok, int64_t C, int64_t ld,
+                            int mode, float thr, const uint32_t* __restrict__ tok_thr,
+                            uint32_t* __restrict__ bits, int64_t ld_bits, int64_t word_off) {
+  const int64_t c = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
+  const int64_t w = blockIdx.y;  // token word
+  if (c >= C) return;
+  uint32_t word = 0;
+  const int64_t t0 = w * 32;
+#pragma unroll 4
+  for (int b = 0; b < 32; ++b) {
+    const int64_t t = t0 + b;
+    if (t >= n_tok) break;
+    const T v = act[t * ld + c];
+    bool on;
+    if (mode == 0) {
+      on = to_f32<T>(v) > thr;
+    } else {
+      uint32_t mag;
+      if constexpr (sizeof(T) == 2) mag = (uint32_t)(*reinterpret_cast<const uint16_t*>(&v)) & 0x7FFFu;
+      else mag = (*reinterpret_cast<const uint32_t*>(&v)) & 0x7FFFFFFFu;
+      on = mag >= tok_thr[t];
+    }
+    word |= (uint32_t)on << b;
+  }
+  bits[c * ld_bits + word_off + w] = word;
+}
+
+// Per-token k-th largest |o| by radix select on magnitude bit patterns
+// (16-bit types: 2 passes of 8 bits; fp32: 4 passes). One CTA per token.
+template <typename T>
+__global__ void topk_threshold_kernel(const T* __restrict__ out, int64_t C, int64_t ld, int64_t k,
+                                      uint32_t* __restrict__ tok_thr) {
+  constexpr int NB = sizeof(T) == 2 ? 16 : 32;
+  __shared__ uint32_t hist[256];
+  __shared__ uint32_t s_prefix, s_k;
+  const T* row = out + int64_t(blockIdx.x) * ld;
+  uint32_t prefix = 0;       // high bits fixed so far
+  uint32_t need = (uint32_t)k;  // rank (1-based, from the top) inside the prefix bucket
+  for (int shift = NB - 8; shift >= 0; shift -= 8) {
+    for (int i = threadIdx.x; i < 256; i += blockDim.x) hist[i] = 0;
+    __syncthreads();
+    const uint32_t hi_mask = (shift + 8 >= 32) ? 0u : (0xFFFFFFFFu << (shift + 8));
+    for (int64_t c = threadIdx.x; c < C; c += blockDim.x) {
+      const T v = row[c];
+      uint32_t mag;
+      if constexpr (sizeof(T) == 2) mag = (uint32_t)(*reinterpret_cast<const uint16_t*>(&v)) & 0x7FFFu;
+      else mag = (*reinterpret_cast<const uint32_t*>(&v)) & 0x7FFFFFFFu;
+      if ((mag & hi_mask) == prefix) atomicAdd(&hist[(mag >> shift) & 0xFF], 1u);
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      uint32_t acc = 0;
+      int d = 255;
+      for (; d > 0; --d) {
+        if (acc + hist[d] >= need) break;
+        acc += hist[d];
+      }
+      s_prefix = prefix | ((uint32_t)d << shift);
+      s_k = need - acc;
+    }
+    __syncthreads();
+    prefix = s_prefix;
+    need = s_k;
+    __syncthreads();
+  }
+  if (threadIdx.x == 0) tok_thr[blockIdx.x] = prefix;
+}
+
+// ── co-activation counts ────────────────────────────────────────────────────
+// 64x64 channel tile per CTA (upper-triangle tiles only, the lower tile is
+// written by transposition); 256 threads each own 4x4 counts (strided by 16);
+// words stream through shared memory 32 at a time.
+constexpr int kTile = 64;
+constexpr int kWordsPerStage = 32;
+
+__global__ void __launch_bounds__(256) coact_kernel(const uint32_t* __restrict__ bits, int64_t C,
+                                                    int64_t n_words, int64_t ld_bits,
+                                                    int32_t* __restrict__ inter, int64_t ld_i,
+                                                    int n_tiles) {
+  // linear upper-triangle tile index -> (ti, tj), ti <= tj
+  int64_t t = blockIdx.x;
+  int ti = 0;
+  while (t >= n_tiles - ti) { t -= n_tiles - ti; ++ti; }
+  const int tj = ti + (int)t;
+  __shared__ uint32_t sa[kWordsPerStage][kTile + 1];
+  __shared__ uint32_t sb[kWordsPerStage][kTile + 1];
+  const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;  // 16 x 16 threads
+  const int64_t i0 = (int64_t)ti * kTile, j0 = (int64_t)tj * kTile;
+  uint32_t acc[4][4];
+#pragma unroll
+  for (int a = 0; a < 4; ++a)
+#pragma unroll
+    for (int b = 0; b < 4; ++b) acc[a][b] = 0;
+  for (int64_t w0 = 0; w0 < n_words; w0 += kWordsPerStage) {
+    // load 64 channels x 32 words for each side
+    for (int e = threadIdx.x; e < kTile * kWordsPerStage; e += blockDim.x) {
+      const int ch = e / kWordsPerStage, ww = e % kWordsPerStage;
+      const int64_t w = w0 + ww;
+      const int64_t ci = i0 + ch, cj = j0 + ch;
+      sa[ww][ch] = (ci < C && w < n_words) ? bits[ci * ld_bits + w] : 0u;
+      sb[ww][ch] = (cj < C && w < n_words) ? bits[cj * ld_bits + w] : 0u;
+    }
+    __syncthreads();
+#pragma unroll 8
+    for (int ww = 0; ww < kWordsPerStage; ++ww) {
+      uint32_t a[4], b[4];
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        a[q] = sa[ww][ty + 16 * q];  // broadcast within a half-warp
+        b[q] = sb[ww][tx + 16 * q];  // 16 consecutive banks
+      }
+#pragma unroll
+      for (int p = 0; p < 4; ++p)
+#pragma unroll
+        for (int q = 0; q < 4; ++q) acc[p][q] += __popc(a[p] & b[q]);
+    }
+    __syncthreads();
+  }
+  // thread (ty, tx) owns rows i0 + ty + 16p and columns j0 + tx + 16q
+#pragma unroll
+  for (int p = 0; p < 4; ++p) {
+    const int64_t i = i0 + ty + 16 * p;
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const int64_t j = j0 + tx + 16 * q;
+      if (i < C && j < C) {
+        inter[i * ld_i + j] = (int32_t)acc[p][q];
+        if (ti != tj) inter[j * ld_i + i] = (int32_t)acc[p][q];
+      }
+    }
+  }
+}
+
+__global__ void popc_rows_kernel(const uint32_t* __restrict__ bits, int64_t C, int64_t n_words,
+                                 int64_t ld_bits, int32_t* __restrict__ f) {
+  const int64_t c = (int64_t(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (c >= C) return;
+  uint32_t s = 0;
+  for (int64_t w = lane; w < n_words; w += 32) s += __popc(bits[c * ld_bits + w]);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+  if (lane == 0) f[c] = (int32_t)s;
+}
+
+// J = I / max(f_i + f_j - I, 1) in fp32 (csaq/core.py:263-265) and the bit
+// J >= thr (thr already rounded to fp32, as torch compares a float32 tensor
+// with a Python float). One warp per 32 columns of one row: ballot -> word.
+__global__ void jaccard_bits_kernel(const int32_t* __restrict__ inter, int64_t ld_i,
+                                    const int32_t* __restrict__ f, int64_t C, float thr,
+                                    uint32_t* __restrict__ adj, int64_t ld_adj) {
+  const int64_t gw = (int64_t(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  const int64_t words_per_row = (C + 31) / 32;
+  if (gw >= C * words_per_row) return;
+  const int64_t i = gw / words_per_row, w = gw % words_per_row;
+  const int64_t j = w * 32 + lane;
+  bool on = false;
+  if (j < C) {
+    const float I = (float)inter[i * ld_i + j];
+    const float uni = fmaxf(__fsub_rn(__fadd_rn((float)f[i], (float)f[j]), I), 1.0f);
+    on = __fdiv_rn(I, uni) >= thr;
+  }
+  const uint32_t word = __ballot_sync(0xffffffffu, on);
+  if (lane == 0) adj[i * ld_adj + w] = word;
+}
+
+// Seed-order greedy partition (csaq/core.py:268-285), one CTA. Channels j < i
+// are always visited when seed i is reached, so clique(i) = {i} + {j > i :
+// adj[i][j] and not visited}. labels[c] = index of c's clique in seed order.
+__global__ void __launch_bounds__(1024) greedy_kernel(const uint32_t* __restrict__ adj,
+                                                      int64_t ld_adj, int C,
+                                                      int32_t* __restrict__ labels,
+                                                      int32_t* __restrict__ n_cliques) {
+  extern __shared__ uint32_t visited[];
+  const int words = (C + 31) / 32;
+  for (int w = threadIdx.x; w < words; w += blockDim.x) visited[w] = 0u;
+  __syncthreads();
+  int id = 0;
+  for (int i = 0; i < C; ++i) {
+    if (visited[i >> 5] & (1u << (i & 31))) continue;  // uniform across the block
+    __syncthreads();
+    const uint32_t* row = adj + (int64_t)i * ld_adj;
+    for (int w = threadIdx.x; w < words; w += blockDim.x) {
+      uint32_t m = row[w] & ~visited[w];
+      if (w == (i >> 5)) m |= 1u << (i & 31);
+      if (w < (i >> 5)) m = 0u;
+      if (m) {
+        visited[w] |= m;
+        while (m) {
+          const int b = __ffs(m) - 1;
+          m &= m - 1;
+          labels[(int64_t)w * 32 + b] = id;
+        }
+      }
+    }
+    ++id;
+    __syncthreads();
+  }
+  if (threadIdx.x == 0) *n_cliques = id;
+}
+
+// ── salience: acc += |G * W| in fp32 (csaq/core.py:204-210) ────────────────
+template <typename T>
+__global__ void salience_kernel(const T* __restrict__ G, const T* __restrict__ W,
+                                float* __restrict__ acc, int64_t n_vec) {
+  constexpr int V = 16 / sizeof(T);
+  const int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i >= n_vec) return;
+  const uint4 g = __ldg(reinterpret_cast<const uint4*>(G) + i);
+  const uint4 w = __ldg(reinterpret_cast<const uint4*>(W) + i);
+  const T* ge = reinterpret_cast<const T*>(&g);
+  const T* we = reinterpret_cast<const T*>(&w);
+  float4* ap = reinterpret_cast<float4*>(acc + i * V);
+#pragma unroll
+  for (int q = 0; q < V / 4; ++q) {
+    float4 a = ap[q];
+    a.x += fabsf(to_f32<T>(ge[4 * q + 0]) * to_f32<T>(we[4 * q + 0]));
+    a.y += fabsf(to_f32<T>(ge[4 * q + 1]) * to_f32<T>(we[4 * q + 1]));
+    a.z += fabsf(to_f32<T>(ge[4 * q + 2]) * to_f32<T>(we[4 * q + 2]));
+    a.w += fabsf(to_f32<T>(ge[4 * q + 3]) * to_f32<T>(we[4 * q + 3]));
+    ap[q] = a;
+  }
+}
+
+template <typename T>
+__global__ void salience_tail_kernel(const T* __restrict__ G, const T* __restrict__ W,
+                                     float* __restrict__ acc, int64_t start, int64_t n) {
+  const int64_t i = start + int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  acc[i] += fabsf(to_f32<T>(G[i]) * to_f32<T>(W[i]));
+}
+
+__global__ void div_kernel(float* __restrict__ a, int64_t n, float d) {
+  const int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i < n) a[i] = __fdiv_rn(a[i], d);
+}
+
+inline int64_t blocks_for(int64_t n) { return (n + kThreads - 1) / kThreads; }
+
+template <typename T>
+int launch_salience(const void* G, const void* W, float* acc, int64_t n, cudaStream_t st) {
+  constexpr int V = 16 / sizeof(T);
+  const bool vec = (reinterpret_cast<uintptr_t>(G) % 16 == 0) && (reinterpret_cast<uintptr_t>(W) % 16 == 0) &&
+                   (reinterpret_cast<uintptr_t>(acc) % 16 == 0);
+  int64_t done = 0;
+  if (vec) {
+    const int64_t nv = n / V;
+    if (nv) salience_kernel<T><<<blocks_for(nv), kThreads, 0, st>>>(
+        reinterpret_cast<const T*>(G), reinterpret_cast<const T*>(W), acc, nv);
+    done = nv * V;
+  }
+  if (done < n)
+    salience_tail_kernel<T><<<blocks_for(n - done), kThreads, 0, st>>>(
+        reinterpret_cast<const T*>(G), reinterpret_cast<const T*>(W), acc, done, n);
+  return launch_status();
+}
+
+}  // namespace
+}  // namespace csaq
+
+using namespace csaq;
+
+extern "C" int csaq_act_mask(const void* act, int dtype, int64_t n_tok, int64_t C, int64_t ld,
+                             int mode, float thr, int64_t k, uint32_t* tok_thr, uint32_t* bits,
+                             int64_t ld_bits, int64_t tok_offset, void* stream) {
+  if (!act || !bits || n_tok < 0 || C <= 0 || ld < C || !dtype_size(dtype)) return CSAQ_ERR_ARG;
+  if (mode != 0 && mode != 1) return CSAQ_ERR_ARG;
+  if (tok_offset % 32 != 0 || ld_bits < (tok_offset + n_tok + 31) / 32) return CSAQ_ERR_ARG;
+  if (mode == 1 && (!tok_thr || k < 1)) return CSAQ_ERR_ARG;
+  if (n_tok == 0) return CSAQ_OK;
+  cudaStream_t st = as_stream(stream);
+  if (mode == 1) {
+    if (k >= C) {
+      mode = 0;  // every channel kept: k >= C gives an all-ones mask
+      thr = -INFINITY;
+    } else {
+      switch (dtype) {
+        case CSAQ_DT_F32: topk_threshold_kernel<float><<<n_tok, 512, 0, st>>>(reinterpret_cast<const float*>(act), C, ld, k, tok_thr); break;
+        case CSAQ_DT_F16: topk_threshold_kernel<__half><<<n_tok, 512, 0, st>>>(reinterpret_cast<const __half*>(act), C, ld, k, tok_thr); break;
+        default: topk_threshold_kernel<__nv_bfloat16><<<n_tok, 512, 0, st>>>(reinterpret_cast<const __nv_bfloat16*>(act), C, ld, k, tok_thr); break;
+      }
+      const int rc = launch_status();
+      if (rc) return rc;
+    }
+  }
+  const dim3 grid((unsigned)((C + kThreads - 1) / kThreads), (unsigned)((n_tok + 31) / 32));
+  const int64_t woff = tok_offset / 32;
+  switch (dtype) {
+    case CSAQ_DT_F32: mask_kernel<float><<<grid, kThreads, 0, st>>>(reinterpret_cast<const float*>(act), n_tok, C, ld, mode, thr, tok_thr, bits, ld_bits, woff); break;
+    case CSAQ_DT_F16: mask_kernel<__half><<<grid, kThreads, 0, st>>>(reinterpret_cast<const __half*>(act), n_tok, C, ld, mode, thr, tok_thr, bits, ld_bits, woff); break;
+    default: mask_kernel<__nv_bfloat16><<<grid, kThreads, 0, st>>>(reinterpret_cast<const __nv_bfloat16*>(act), n_tok, C, ld, mode, thr, tok_thr, bits, ld_bits, woff); break;
+  }
+  return launch_status();
+}
+
+extern "C" int csaq_coact_counts(const uint32_t* bits, int64_t C, int64_t n_words, int64_t ld_bits,
+                                 int32_t* inter, int64_t ld_i, int32_t* f, void* stream) {
+  if (!bits || !inter || C <= 0 || n_words < 0 || ld_bits < n_words || ld_i < C) return CSAQ_ERR_ARG;
+  cudaStream_t st = as_stream(stream);
+  const int n_tiles = (int)((C + kTile - 1) / kTile);
+  const int64_t n_blocks = (int64_t)n_tiles * (n_tiles + 1) / 2;
+  coact_kernel<<<n_blocks, 256, 0, st>>>(bits, C, n_words, ld_bits, inter, ld_i, n_tiles);
+  int rc = launch_status();
+  if (rc || !f) return rc;
+  popc_rows_kernel<<<blocks_for(C * 32), kThreads, 0, st>>>(bits, C, n_words, ld_bits, f);
+  return launch_status();
+}
+
+extern "C" int csaq_jaccard_bits(const int32_t* inter, int64_t ld_i, const int32_t* f, int64_t C,
+                                 float threshold, uint32_t* adj, int64_t ld_adj, void* stream) {
+  if (!inter || !f || !adj || C <= 0 || ld_i < C || ld_adj < (C + 31) / 32) return CSAQ_ERR_ARG;
+  const int64_t warps = C * ((C + 31) / 32);
+  jaccard_bits_kernel<<<blocks_for(warps * 32), kThreads, 0, as_stream(stream)>>>(
+      inter, ld_i, f, C, threshold, adj, ld_adj);
+  return launch_status();
+}
+
+extern "C" int csaq_greedy_cliques(const uint32_t* adj, int64_t ld_adj, int64_t C, int32_t* labels,
+                                   int32_t* n_cliques, void* stream) {
+  if (!adj || !labels || !n_cliques || C <= 0 || ld_adj < (C + 31) / 32) return CSAQ_ERR_ARG;
+  const int64_t words = (C + 31) / 32;
+  if (words * 4 > 200 * 1024) return CSAQ_ERR_UNSUPPORTED;  // visited set lives in shared memory
+  const size_t smem = (size_t)words * 4;
+  if (smem > 48 * 1024) {
+    if (cudaFuncSetAttribute(greedy_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
+      return launch_status();
+  }
+  greedy_kernel<<<1, 1024, smem, as_stream(stream)>>>(adj, ld_adj, (int)C, labels, n_cliques);
+  return launch_status();
+}
+
+extern "C" int csaq_salience_accum(const void* G, const void* W, int dtype, int64_t n, float* acc,
+                                   void* stream) {
+  if (!G || !W || !acc || n < 0 || !dtype_size(dtype)) return CSAQ_ERR_ARG;
+  if (n == 0) return CSAQ_OK;
+  cudaStream_t st = as_stream(stream);
+  switch (dtype) {
+    case CSAQ_DT_F32: return launch_salience<float>(G, W, acc, n, st);
+    case CSAQ_DT_F16: return launch_salience<__half>(G, W, acc, n, st);
+    default: return launch_salience<__nv_bfloat16>(G, W, acc, n, st);
+  }
+}
+
+extern "C" int csaq_salience_finalize(float* acc, int64_t n, int64_t n_batches, void* stream) {
+  if (!acc || n < 0 || n_batches < 1) return CSAQ_ERR_ARG;
+  if (n == 0) return CSAQ_OK;
+  div_kernel<<<blocks_for(n), kThreads, 0, as_stream(stream)>>>(acc, n, (float)n_batches);
+  return launch_status();
+}

@@ -1,0 +1,102 @@
+// Shared device helpers for the csaq B200 kernels.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <cuda_fp16.h>
+#include <cuda_bf16.h>
+#include <stdint.h>
+
+#include "csaq_b200.h"
+
+namespace csaq {
+
+// Thread-local record of the last CUDA launch error (csaq_last_cuda_error).
+void set_last_cuda_error(cudaError_t e);
+
+inline int launch_status() {
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) {
+    set_last_cuda_error(e);
+    return CSAQ_ERR_CUDA;
+  }
+  return CSAQ_OK;
+}
+
+inline cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s); }
+
+inline int dtype_size(int dt) {
+  switch (dt) {
+    case CSAQ_DT_F32: return 4;
+    case CSAQ_DT_F16: return 2;
+    case CSAQ_DT_BF16: return 2;
+    default: return 0;
+  }
+}
+
+inline int64_t packed_row_bytes(int64_t cols, int bits) {
+  switch (bits) {
+    case 8: return cols;
+    case 4: return (cols + 1) / 2;
+    case 2: return (cols + 3) / 4;
+    case 16: return cols * 2;
+    default: return -1;
+  }
+}
+
+// Exact widening of one element to fp32.
+__device__ __forceinline__ float load_as_f32(const void* p, int dt, int64_t i) {
+  if (dt == CSAQ_DT_F32) return reinterpret_cast<const float*>(p)[i];
+  if (dt == CSAQ_DT_F16) return __half2float(reinterpret_cast<const __half*>(p)[i]);
+  return __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(p)[i]);
+}
+
+template <typename T> __device__ __forceinline__ float to_f32(T v);
+template <> __device__ __forceinline__ float to_f32<float>(float v) { return v; }
+template <> __device__ __forceinline__ float to_f32<__half>(__half v) { return __half2float(v); }
+template <> __device__ __forceinline__ float to_f32<__nv_bfloat16>(__nv_bfloat16 v) {
+  return __bfloat162float(v);
+}
+
+template <typename T> __device__ __forceinline__ T from_f32(float v);
+template <> __device__ __forceinline__ float from_f32<float>(float v) { return v; }
+template <> __device__ __forceinline__ __half from_f32<__half>(float v) { return __float2half_rn(v); }
+template <> __device__ __forceinline__ __nv_bfloat16 from_f32<__nv_bfloat16>(float v) {
+  return __float2bfloat16_rn(v);
+}
+
+// ── torch CPU arithmetic, one IEEE rounding per op ─────────────────────────
+// torch.clamp propagates NaN (fminf/fmaxf would drop it).
+__device__ __forceinline__ float clamp_nan(float v, float lo, float hi) {
+  if (v != v) return v;
+  return fminf(fmaxf(v, lo), hi);
+}
+
+// .to(torch.int32) on x86: truncation; NaN and out-of-range give INT32_MIN.
+__device__ __forceinline__ int32_t to_i32_x86(float v) {
+  if (!(v >= -2147483648.0f && v < 2147483648.0f)) return INT32_MIN;
+  return __float2int_rz(v);
+}
+
+// _compute_scale_zp for one (min, max) pair (csaq/kernels.py:495-508).
+__device__ __forceinline__ void scale_zp(float w_min, float w_max, int bits, float& scale,
+                                         int32_t& zp) {
+  const float n_levels = (float)((1 << bits) - 1);
+  if (!(w_max > w_min)) w_max = __fadd_rn(w_min, 1e-8f);
+  scale = __fdiv_rn(__fsub_rn(w_max, w_min), n_levels);
+  const float z = rintf(__fdiv_rn(-w_min, scale));
+  zp = to_i32_x86(clamp_nan(z, 0.0f, n_levels));
+}
+
+// _quantize_rows for one element (csaq/kernels.py:511-523).
+__device__ __forceinline__ int32_t quant_one(float w, float scale, int32_t zp, int bits) {
+  const float n_levels = (float)((1 << bits) - 1);
+  const float v = rintf(__fadd_rn(__fdiv_rn(w, scale), (float)zp));
+  return to_i32_x86(clamp_nan(v, 0.0f, n_levels));
+}
+
+// (q - zp) * scale in fp32 (csaq/kernels.py:611, 619, 465).
+__device__ __forceinline__ float dequant_one(int32_t q, int32_t zp, float scale) {
+  return __fmul_rn(__fsub_rn((float)q, (float)zp), scale);
+}
+
+}  // namespace csaq

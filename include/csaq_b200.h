@@ -1,0 +1,195 @@
+/*
+ * csaq_b200.h — C ABI of the B200 (sm_100a) quantised hot path of csaq-quant.
+ *
+ * Every entry point is stream-ordered (enqueues work on `stream`, a
+ * cudaStream_t passed as void*), never synchronises, never allocates, and
+ * returns an int status (CSAQ_OK = 0, negative on error). Buffers are
+ * caller-owned device pointers. Sizes are int64_t. Layouts are row-major.
+ *
+ * Packed-code layout (identical to csaq-quant's storage):
+ *   bits 8: one byte per code;   bits 4: byte j = col 2j (low nibble) | col 2j+1 (high);
+ *   bits 2: byte j holds cols 4j..4j+3 at bit offsets 0,2,4,6;
+ *   bits 16: the fp16 bit pattern, 2 bytes per column.
+ *   packed row length = ceil(cols * bits / 8) bytes.
+ * Scales are fp32 and zero points int32, one per (row, group); per-channel
+ * quantisation has one group per row.
+ */
+#ifndef CSAQ_B200_H
+#define CSAQ_B200_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum {
+  CSAQ_OK = 0,
+  CSAQ_ERR_ARG = -1,          /* null pointer, bad size, bad dtype            */
+  CSAQ_ERR_BITS = -2,         /* unsupported bit-width                          */
+  CSAQ_ERR_CUDA = -3,         /* a CUDA launch failed; see csaq_last_cuda_error */
+  CSAQ_ERR_TIMEOUT = -4,      /* a bounded device wait gave up                  */
+  CSAQ_ERR_UNSUPPORTED = -5,  /* shape/alignment outside what the kernel serves */
+};
+
+enum { CSAQ_DT_F32 = 0, CSAQ_DT_F16 = 1, CSAQ_DT_BF16 = 2 };
+
+/* Library identification and diagnostics. */
+const char* csaq_version(void);
+const char* csaq_status_string(int status);
+int csaq_last_cuda_error(void);   /* cudaError_t of the last failed launch in this thread */
+
+/* ── Quantisation primitives ─────────────────────────────────────────────── */
+
+/* Packed bytes per row: replaces the cols_packed arithmetic of
+ * csaq/kernels.py:336-345 and the shapes produced by _pack (csaq/kernels.py:539-569). */
+int64_t csaq_packed_row_bytes(int64_t cols, int bits);
+
+/* Per-(row, group) asymmetric scale and zero point from min/max:
+ * csaq/kernels.py:495-508 (_compute_scale_zp) on the per-channel
+ * (csaq/kernels.py:113-118) or zero-padded per-group (csaq/kernels.py:129-138)
+ * statistics. group_size <= 0 or >= cols selects per-channel (one group, no
+ * padding). scales/zero_points: rows x n_groups. row_absmax (nullable): max |W|
+ * per row, used for the follower-outlier warning of csaq/kernels.py:208-218. */
+int csaq_group_scales(const void* W, int w_dtype, int64_t rows, int64_t cols, int64_t ld_w,
+                      int bits, int64_t group_size, float* scales, int32_t* zero_points,
+                      float* row_absmax, void* stream);
+
+/* Quantise + pack with given scales: csaq/kernels.py:511-523 (_quantize_rows) then
+ * csaq/kernels.py:539-569 (_pack).
+ * scale_mode 0: row r uses scales[r, :]; 1: every row uses row 0 (shared scale,
+ * csaq/kernels.py:220-223, 247-252); 2: row r uses row src_row[r].
+ * requant != 0 reproduces CSAQLinear.from_cliques (csaq/kernels.py:414-434):
+ * dequantise (q - zp) * scale in fp32, then _float_to_int (csaq/kernels.py:526-536). */
+int csaq_quant_pack_rows(const void* W, int w_dtype, int64_t rows, int64_t cols, int64_t ld_w,
+                         int bits, int64_t group_size, const float* scales,
+                         const int32_t* zero_points, int64_t ld_s, int scale_mode,
+                         const int32_t* src_row, int requant, uint8_t* qdata, void* stream);
+
+/* quantize_per_channel (csaq/kernels.py:77-158) for bits 2/4/8: scales +
+ * codes in one pass where the group layout allows it (fused warp-per-group
+ * kernel with 128-bit loads and shuffle min/max), else csaq_group_scales +
+ * csaq_quant_pack_rows. */
+int csaq_quant_pack(const void* W, int w_dtype, int64_t rows, int64_t cols, int64_t ld_w,
+                    int bits, int64_t group_size, uint8_t* qdata, float* scales,
+                    int32_t* zero_points, void* stream);
+
+/* quantize_per_channel(bits=16): the fp16 cast (csaq/kernels.py:94-107). */
+int csaq_cast_f16(const void* W, int w_dtype, int64_t rows, int64_t cols, int64_t ld_w,
+                  uint16_t* out, void* stream);
+
+/* _pack (csaq/kernels.py:539-569): int32 codes -> packed bytes (low byte kept). */
+int csaq_pack(const int32_t* q, int bits, int64_t rows, int64_t cols, uint8_t* out, void* stream);
+
+/* _unpack (csaq/kernels.py:572-600): packed bytes -> int32 codes. */
+int csaq_unpack(const uint8_t* packed, int bits, int64_t rows, int64_t cols, int32_t* out,
+                void* stream);
+
+/* _float_to_int (csaq/kernels.py:526-536): row-wise requantisation to int32 codes. */
+int csaq_float_to_int(const float* W, const float* scales, const int32_t* zero_points, int bits,
+                      int64_t rows, int64_t cols, int32_t* out, void* stream);
+
+/* _dequantize (csaq/kernels.py:603-619) and CSAQLinear._get_weight_fp32
+ * (csaq/kernels.py:450-468): (q - zp) * scale in fp32, bit-exact; column c
+ * uses group c / group_size (group_size <= 0: per-channel). bits 16 reads fp16.
+ * nan_to_num != 0 applies csaq/kernels.py:467. out_dtype F16/BF16 rounds the
+ * fp32 value once (the .to(x.dtype) of csaq/kernels.py:471). */
+int csaq_dequant(const uint8_t* qdata, const float* scales, const int32_t* zero_points, int bits,
+                 int64_t rows, int64_t cols, int64_t group_size, int nan_to_num, int out_dtype,
+                 void* out, void* stream);
+
+/* ── Mixed-precision quantised linear ────────────────────────────────────── */
+
+/* One row tier of a mixed linear: rows stored at one bit-width. A linear is a
+ * list of tiers; several linears that read the same activation (q/k/v,
+ * gate/up) can share one launch. The verify pass of self-speculative decoding
+ * is the same launch with each tier's protected rows left out (n_rows covers
+ * only the unprotected head of the tier) plus a 16-bit tier holding the fp16
+ * backups of the protected rows, scattered to their output rows.
+ * Replaces CSAQLinear._get_weight_fp32 + F.linear (csaq/kernels.py:450-475)
+ * and the verify weight swap (csaq/inference.py:219-237). */
+typedef struct csaq_tier {
+  int32_t bits;            /* 2, 4, 8, or 16 (fp16 rows)                       */
+  int32_t n_rows;          /* rows computed from this tier                     */
+  int32_t group_size;      /* columns per scale group (K for per-channel)      */
+  int32_t n_groups;        /* scale/zp columns per row                         */
+  int64_t row_bytes;       /* byte stride between packed rows                  */
+  const uint8_t* codes;    /* n_rows x row_bytes                               */
+  const float* scales;     /* n_rows x n_groups (ignored for bits 16)          */
+  const uint8_t* zps;      /* n_rows x n_groups, zero points as uint8          */
+  const int32_t* out_rows; /* output column of y for each tier row             */
+  const uint8_t* blocks;   /* nullable: the tier repacked by csaq_repack_tiles;
+                              the tensor-core kernel reads only this           */
+  void* y;                 /* output, M x ldy, activation dtype                */
+  int64_t ldy;
+  const void* bias;        /* nullable; indexed by output row, activation dtype */
+  const void* residual;    /* nullable; M x ldr, activation dtype: y = residual + W x */
+  int64_t ldr;
+} csaq_tier;
+
+#define CSAQ_MAX_TIERS 16
+
+/* GEMV block layout of a tier: one contiguous block per (16-row tile,
+ * 128-column chunk), tile-major; inside a block the codes are ordered by the
+ * MMA lane that consumes them, followed by the 16 rows' fp32 scales and uint8
+ * zero points of that chunk's group (rows past n_rows are zero). Built once
+ * per layer from the reference layout; K must be a multiple of 128 and the
+ * group size a power-of-two multiple of 128 (or per-channel). */
+int64_t csaq_tile_blocks_bytes(int bits, int64_t n_rows, int64_t K);
+int csaq_repack_tiles(const csaq_tier* tier, int64_t K, uint8_t* blocks, void* stream);
+
+/* y[m, out_rows[i]] = residual + sum_k W[i, k] * x[m, k] + bias, fp32
+ * accumulation; x is M x ldx in x_dtype (F32, F16 or BF16), y and bias and
+ * residual in the same dtype. F16/BF16 use the tensor-core kernel when every
+ * tier with rows has `blocks` (csaq_repack_tiles) and x is 16-byte aligned
+ * with ldx % 8 == 0; everything else (and F32) uses the CUDA-core kernel,
+ * which reads the reference layout (`codes`, `scales`, `zps`). */
+int csaq_qgemv(const csaq_tier* tiers, int n_tiers, int64_t K, const void* x, int x_dtype,
+               int64_t M, int64_t ldx, void* stream);
+
+/* Same contract, always the CUDA-core kernel (any K, any group size, any M);
+ * a second GPU path used to cross-check the tensor-core kernel. */
+int csaq_qgemv_simt(const csaq_tier* tiers, int n_tiers, int64_t K, const void* x, int x_dtype,
+                    int64_t M, int64_t ldx, void* stream);
+
+
+/* ── Calibration ─────────────────────────────────────────────────────────── */
+
+/* Co-activation mask of one activation block (n_tok x C, row stride ld),
+ * bit-packed channel-major: bits[c * ld_bits + (tok_offset + t) / 32] bit
+ * (tok_offset + t) % 32. tok_offset must be a multiple of 32.
+ * mode 0: act > thr (thr given in the activation dtype's value).
+ * mode 1: the profiler hook of csaq/core.py:143-155: per token keep channels
+ *         with |act| >= the k-th largest |act| (ties kept); tok_thr is an
+ *         n_tok scratch array of uint32 written by the call. */
+int csaq_act_mask(const void* act, int dtype, int64_t n_tok, int64_t C, int64_t ld, int mode,
+                  float thr, int64_t k, uint32_t* tok_thr, uint32_t* bits, int64_t ld_bits,
+                  int64_t tok_offset, void* stream);
+
+/* Intersection counts inter[i][j] = popc(mask_i & mask_j) summed over words
+ * (the exact integers of mask^T mask, csaq/core.py:261-262) and activation
+ * counts f[i] (csaq/core.py:263; nullable). */
+int csaq_coact_counts(const uint32_t* bits, int64_t C, int64_t n_words, int64_t ld_bits,
+                      int32_t* inter, int64_t ld_i, int32_t* f, void* stream);
+
+/* Jaccard threshold bits: adj[i] bit j = (I/max(f_i+f_j-I, 1) >= threshold) in
+ * fp32 (csaq/core.py:263-275); threshold is the fp32-rounded value. */
+int csaq_jaccard_bits(const int32_t* inter, int64_t ld_i, const int32_t* f, int64_t C,
+                      float threshold, uint32_t* adj, int64_t ld_adj, void* stream);
+
+/* Seed-order greedy clique partition (csaq/core.py:268-285) on one CTA:
+ * labels[c] = clique index of channel c in seed order; *n_cliques = count. */
+int csaq_greedy_cliques(const uint32_t* adj, int64_t ld_adj, int64_t C, int32_t* labels,
+                        int32_t* n_cliques, void* stream);
+
+/* Salience accumulation acc += |G * W| in fp32 over n contiguous elements
+ * (csaq/core.py:204-210), and the final acc /= n_batches (csaq/core.py:232-233). */
+int csaq_salience_accum(const void* G, const void* W, int dtype, int64_t n, float* acc,
+                        void* stream);
+int csaq_salience_finalize(float* acc, int64_t n, int64_t n_batches, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* CSAQ_B200_H */

@@ -1,0 +1,84 @@
+"""The C-ABI library loads and exports every entry point declared in include/*.h.
+
+Runs without a GPU: only symbol lookup and argument validation paths that
+return before any launch are exercised.
+"""
+
+import ctypes
+import glob
+import os
+import re
+
+import pytest
+
+from conftest import REPO
+
+
+def _declared_functions():
+    names = set()
+    for h in glob.glob(os.path.join(REPO, "include", "*.h")):
+        src = open(h).read()
+        src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
+        for m in re.finditer(r"^\s*(?:const\s+)?[a-z_0-9]+\s*\*?\s+(csaq_[a-z0-9_]+)\s*\(", src, re.M):
+            names.add(m.group(1))
+    return sorted(names)
+
+
+def test_header_declares_entry_points():
+    names = _declared_functions()
+    for expected in ("csaq_quant_pack", "csaq_dequant", "csaq_qgemv", "csaq_unpack"):
+        assert expected in names
+
+
+def test_library_exports_every_declared_symbol():
+    from csaq import _lib
+    L = _lib.lib()
+    missing = [n for n in _declared_functions() if not hasattr(L, n)]
+    assert not missing, missing
+
+
+def test_python_binding_covers_every_declared_symbol():
+    from csaq import _lib
+    _lib.lib()
+    declared = set(_declared_functions())
+    bound = set(_lib.exported_symbols())
+    assert declared <= bound, sorted(declared - bound)
+
+
+def test_version_and_status_strings():
+    from csaq import _lib
+    L = _lib.lib()
+    assert b"sm_100a" in L.csaq_version()
+    assert L.csaq_status_string(0) == b"ok"
+    assert L.csaq_status_string(-2) == b"unsupported bit-width"
+    assert L.csaq_packed_row_bytes(37, 4) == 19
+    assert L.csaq_packed_row_bytes(37, 2) == 10
+    assert L.csaq_packed_row_bytes(37, 8) == 37
+    assert L.csaq_packed_row_bytes(37, 16) == 74
+    assert L.csaq_packed_row_bytes(37, 3) == -1
+
+
+def test_argument_validation_without_launch():
+    """Bad arguments are rejected on the host before any kernel launch."""
+    from csaq import _lib
+    L = _lib.lib()
+    dummy = ctypes.c_void_p(16)
+    assert L.csaq_quant_pack(None, 0, 4, 4, 4, 4, 128, dummy, dummy, dummy, None) == -1
+    assert L.csaq_quant_pack(dummy, 0, 4, 4, 4, 3, 128, dummy, dummy, dummy, None) == -2
+    assert L.csaq_quant_pack(dummy, 7, 4, 4, 4, 4, 128, dummy, dummy, dummy, None) == -1
+    assert L.csaq_unpack(dummy, 5, 4, 4, dummy, None) == -2
+    assert L.csaq_dequant(dummy, None, None, 4, 4, 4, -1, 0, 0, dummy, None) == -1
+    t = _lib.CsaqTier(bits=3, n_rows=1, group_size=128, n_groups=1, row_bytes=64)
+    arr = _lib.tier_array([t])
+    assert L.csaq_qgemv(arr, 1, 128, dummy, 2, 1, 128, None) == -2
+    assert L.csaq_qgemv(arr, 0, 128, dummy, 2, 1, 128, None) == -1
+    assert L.csaq_qgemv(arr, 17, 128, dummy, 2, 1, 128, None) == -1
+
+
+def test_kernels_fail_loudly_without_cuda():
+    import torch
+    if torch.cuda.is_available():
+        pytest.skip("a CUDA device is present")
+    from csaq.kernels import quantize_per_channel
+    with pytest.raises(RuntimeError, match="CUDA"):
+        quantize_per_channel(torch.randn(4, 8), 4)
