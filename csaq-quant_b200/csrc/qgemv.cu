@@ -93,8 +93,6 @@ template <int BITS> struct Geo {
   static constexpr int kCodeBytes = 16 * 16 * BITS;         // 16 rows x 128 columns
   static constexpr int kMetaBytes = BITS == 16 ? 0 : 80;
   static constexpr int kBlockBytes = (kCodeBytes + kMetaBytes + 15) / 16 * 16;
-  // ring slots per warp (about 9 KB in flight per warp)
-  static constexpr int kDepth = BITS == 2 ? 12 : BITS == 4 ? 8 : BITS == 8 ? 4 : 2;
 };
 
 __host__ __device__ __forceinline__ int block_bytes(int bits) {
@@ -212,58 +210,76 @@ __device__ __forceinline__ void build_records(const ACT* __restrict__ xrow, floa
   S = s;
 }
 
-// MMA over one chunk for rows g and g+8 of the lane: g4 += A * B.
-template <int BITS>
-__device__ __forceinline__ void chunk_mma(const uint32_t (&cw)[2][BITS], const uint2 (&rec)[8],
-                                          float (&g)[4]) {
+// MMA over one chunk for the MT tiles of an item (rows g and g+8 of each):
+// the tiles' MMAs are interleaved and each tile alternates between two
+// accumulators, so 2*MT independent chains share the tensor pipe.
+template <int BITS, int MT>
+__device__ __forceinline__ void chunk_mma(const uint32_t (&cw)[MT][2][BITS], const uint2 (&rec)[8],
+                                          float (&g)[MT][2][4]) {
   constexpr uint32_t M = 0x64006400u;  // fp16 1024.0 in both halves
   if constexpr (BITS == 4) {
 #pragma unroll
     for (int m = 0; m < 4; ++m) {
-      uint32_t v[2][4];
+      uint32_t v[MT][2][4];
 #pragma unroll
-      for (int r = 0; r < 2; ++r) {
-        const uint32_t w = cw[r][m], t = w >> 8;
-        v[r][0] = lop_and_or(w, 0x000F000Fu, M);  // 1024 + q   (cols 0, 4)
-        v[r][1] = lop_and_or(w, 0x00F000F0u, M);  // 1024 + 16q (cols 1, 5)
-        v[r][2] = lop_and_or(t, 0x000F000Fu, M);  //             (cols 2, 6)
-        v[r][3] = lop_and_or(t, 0x00F000F0u, M);  //             (cols 3, 7)
-      }
-      mma_f16(g, v[0][0], v[1][0], v[0][1], v[1][1], rec[2 * m].x, rec[2 * m].y);
-      mma_f16(g, v[0][2], v[1][2], v[0][3], v[1][3], rec[2 * m + 1].x, rec[2 * m + 1].y);
+      for (int mt = 0; mt < MT; ++mt)
+#pragma unroll
+        for (int r = 0; r < 2; ++r) {
+          const uint32_t w = cw[mt][r][m], t = w >> 8;
+          v[mt][r][0] = lop_and_or(w, 0x000F000Fu, M);  // 1024 + q   (cols 0, 4)
+          v[mt][r][1] = lop_and_or(w, 0x00F000F0u, M);  // 1024 + 16q (cols 1, 5)
+          v[mt][r][2] = lop_and_or(t, 0x000F000Fu, M);  //             (cols 2, 6)
+          v[mt][r][3] = lop_and_or(t, 0x00F000F0u, M);  //             (cols 3, 7)
+        }
+#pragma unroll
+      for (int mt = 0; mt < MT; ++mt)
+        mma_f16(g[mt][0], v[mt][0][0], v[mt][1][0], v[mt][0][1], v[mt][1][1], rec[2 * m].x, rec[2 * m].y);
+#pragma unroll
+      for (int mt = 0; mt < MT; ++mt)
+        mma_f16(g[mt][1], v[mt][0][2], v[mt][1][2], v[mt][0][3], v[mt][1][3], rec[2 * m + 1].x, rec[2 * m + 1].y);
     }
   } else if constexpr (BITS == 8) {
 #pragma unroll
     for (int m = 0; m < 8; ++m) {
-      const uint32_t a0 = prmt(cw[0][m], 0x64646464u, 0x4240), a1 = prmt(cw[1][m], 0x64646464u, 0x4240);
-      const uint32_t a2 = prmt(cw[0][m], 0x64646464u, 0x4341), a3 = prmt(cw[1][m], 0x64646464u, 0x4341);
-      mma_f16(g, a0, a1, a2, a3, rec[m].x, rec[m].y);
+#pragma unroll
+      for (int mt = 0; mt < MT; ++mt) {
+        const uint32_t a0 = prmt(cw[mt][0][m], 0x64646464u, 0x4240), a1 = prmt(cw[mt][1][m], 0x64646464u, 0x4240);
+        const uint32_t a2 = prmt(cw[mt][0][m], 0x64646464u, 0x4341), a3 = prmt(cw[mt][1][m], 0x64646464u, 0x4341);
+        mma_f16(g[mt][m & 1], a0, a1, a2, a3, rec[m].x, rec[m].y);
+      }
     }
   } else if constexpr (BITS == 2) {
 #pragma unroll
     for (int m = 0; m < 2; ++m) {
-      uint32_t v[2][8];
+      uint32_t v[MT][2][8];
 #pragma unroll
-      for (int r = 0; r < 2; ++r) {
-        const uint32_t w = cw[r][m], t = w >> 8;
-        v[r][0] = lop_and_or(w, 0x00030003u, M);
-        v[r][1] = lop_and_or(w, 0x000C000Cu, M);
-        v[r][2] = lop_and_or(w, 0x00300030u, M);
-        v[r][3] = lop_and_or(w, 0x00C000C0u, M);
-        v[r][4] = lop_and_or(t, 0x00030003u, M);
-        v[r][5] = lop_and_or(t, 0x000C000Cu, M);
-        v[r][6] = lop_and_or(t, 0x00300030u, M);
-        v[r][7] = lop_and_or(t, 0x00C000C0u, M);
-      }
+      for (int mt = 0; mt < MT; ++mt)
+#pragma unroll
+        for (int r = 0; r < 2; ++r) {
+          const uint32_t w = cw[mt][r][m], t = w >> 8;
+          v[mt][r][0] = lop_and_or(w, 0x00030003u, M);
+          v[mt][r][1] = lop_and_or(w, 0x000C000Cu, M);
+          v[mt][r][2] = lop_and_or(w, 0x00300030u, M);
+          v[mt][r][3] = lop_and_or(w, 0x00C000C0u, M);
+          v[mt][r][4] = lop_and_or(t, 0x00030003u, M);
+          v[mt][r][5] = lop_and_or(t, 0x000C000Cu, M);
+          v[mt][r][6] = lop_and_or(t, 0x00300030u, M);
+          v[mt][r][7] = lop_and_or(t, 0x00C000C0u, M);
+        }
 #pragma unroll
       for (int t = 0; t < 4; ++t)
-        mma_f16(g, v[0][2 * t], v[1][2 * t], v[0][2 * t + 1], v[1][2 * t + 1], rec[4 * m + t].x,
-                rec[4 * m + t].y);
+#pragma unroll
+        for (int mt = 0; mt < MT; ++mt)
+          mma_f16(g[mt][t & 1], v[mt][0][2 * t], v[mt][1][2 * t], v[mt][0][2 * t + 1], v[mt][1][2 * t + 1],
+                  rec[4 * m + t].x, rec[4 * m + t].y);
     }
   } else {
 #pragma unroll
     for (int s = 0; s < 8; ++s)
-      mma_f16(g, cw[0][2 * s], cw[1][2 * s], cw[0][2 * s + 1], cw[1][2 * s + 1], rec[s].x, rec[s].y);
+#pragma unroll
+      for (int mt = 0; mt < MT; ++mt)
+        mma_f16(g[mt][s & 1], cw[mt][0][2 * s], cw[mt][1][2 * s], cw[mt][0][2 * s + 1], cw[mt][1][2 * s + 1],
+                rec[s].x, rec[s].y);
   }
 }
 
@@ -279,46 +295,67 @@ struct KParams {
   int cta_start[CSAQ_MAX_TIERS + 1];  // persistent CTAs per tier
 };
 
+// Tiles per work item: two 16-row tiles share each chunk's activation
+// records and give two independent MMA chains; fp16 tiers keep one (their
+// blocks are already 4 KB).
+template <int BITS> struct Item {
+  static constexpr int kTiles = BITS == 16 ? 1 : 2;
+  static constexpr int kBytes = kTiles * Geo<BITS>::kBlockBytes;
+  static constexpr int kDepth = BITS == 2 ? 8 : BITS == 4 ? 4 : 2;  // ring slots per warp
+};
+
+__host__ __device__ __forceinline__ int item_tiles(int bits) { return bits == 16 ? 1 : 2; }
+
 template <typename ACT, int NT, int BITS>
 __device__ __forceinline__ void run_tier(const csaq_tier& T, int cta_in_tier, int ctas_in_tier,
                                          int64_t K, const ACT* __restrict__ x, int M, int64_t ldx,
                                          uint8_t* smem, const LaunchCfg& cfg) {
   using G = Geo<BITS>;
-  const int depth = G::kDepth / cfg.ring_div;
+  using I = Item<BITS>;
+  constexpr int MT = I::kTiles;
+  const int depth = I::kDepth / cfg.ring_div;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane >> 2, c = lane & 3;
   const int n_chunks = (int)(K / 128);
   const int n_tiles = (T.n_rows + kTileRows - 1) / kTileRows;
-  const int my_tiles = cta_in_tier < n_tiles ? (n_tiles - 1 - cta_in_tier) / ctas_in_tier + 1 : 0;
-  const int cpw = (n_chunks + kWarps - 1) / kWarps;  // items per warp per tile (uniform)
-  const int total = my_tiles * cpw;
+  const int n_units = (n_tiles + MT - 1) / MT;
+  const int my_units = cta_in_tier < n_units ? (n_units - 1 - cta_in_tier) / ctas_in_tier + 1 : 0;
+  const int cpw = (n_chunks + kWarps - 1) / kWarps;  // items per warp per unit (uniform)
+  const int total = my_units * cpw;
+  constexpr int kRows = MT * kTileRows;
 
   uint2* xrec = reinterpret_cast<uint2*>(smem);                               // [ch][8][M][4]
   float2* xcs = reinterpret_cast<float2*>(smem + cfg.x_bytes);                // [ch][M] (C, S)
   float* xexp = reinterpret_cast<float*>(smem + cfg.x_bytes + cfg.cs_bytes);  // [16] 2^e per token
-  float* red = xexp + 16;                                                     // [warps][16][NT*8]
-  uint8_t* ring = reinterpret_cast<uint8_t*>(red + kWarps * kTileRows * NT * 8) +
-                  (size_t)warp * depth * G::kBlockBytes;
+  float* red = xexp + 16;                                                     // [warps][kRows][NT*8]
+  uint8_t* ring = reinterpret_cast<uint8_t*>(red + kWarps * 32 * NT * 8) +
+                  (size_t)warp * depth * I::kBytes;
 
-  // issue cursor: the warp's blocks are chunks warp, warp+8, ... of each tile
-  int i_it = 0, i_j = 0, i_slot = 0;
-  const uint8_t* i_src = T.blocks + ((int64_t)cta_in_tier * n_chunks + warp) * G::kBlockBytes;
-  const int64_t tile_stride = (int64_t)ctas_in_tier * n_chunks * G::kBlockBytes;
+  // issue cursor: unit u covers tiles u*MT .. u*MT+MT-1; the warp's items are
+  // chunks warp, warp+8, ... of each of its units
+  int i_it = 0, i_j = 0, i_slot = 0, i_unit = cta_in_tier;
   auto issue = [&]() {
     if (i_it < total) {
-      if (warp + kWarps * i_j < n_chunks) {
-        uint8_t* slot = ring + i_slot * G::kBlockBytes;
+      const int ch = warp + kWarps * i_j;
+      if (ch < n_chunks) {
+        uint8_t* slot = ring + i_slot * I::kBytes;
 #pragma unroll
-        for (int off = 0; off < G::kBlockBytes; off += 512)
-          if (off + lane * 16 < G::kBlockBytes) cp_async16(slot + off + lane * 16, i_src + off + lane * 16);
+        for (int mt = 0; mt < MT; ++mt) {
+          const int tile = i_unit * MT + mt;
+          if (tile < n_tiles) {
+            const uint8_t* src = T.blocks + ((int64_t)tile * n_chunks + ch) * G::kBlockBytes;
+            uint8_t* dst = slot + mt * G::kBlockBytes;
+#pragma unroll
+            for (int off = 0; off < G::kBlockBytes; off += 512)
+              if (off + lane * 16 < G::kBlockBytes) cp_async16(dst + off + lane * 16, src + off + lane * 16);
+          }
+        }
       }
       ++i_it;
       i_slot = (i_slot + 1 == depth) ? 0 : i_slot + 1;
       if (++i_j == cpw) {
         i_j = 0;
-        i_src += tile_stride - (int64_t)(cpw - 1) * kWarps * G::kBlockBytes;
-      } else {
-        i_src += (int64_t)kWarps * G::kBlockBytes;
+        i_unit += ctas_in_tier;
       }
     }
     cp_async_commit();
@@ -350,10 +387,10 @@ __device__ __forceinline__ void run_tier(const csaq_tier& T, int cta_in_tier, in
   __syncthreads();
 
   // stage activation records; whole warps iterate together (4-lane shuffles)
-  const int n_units = M * n_chunks * 4;
-  for (int base = 0; base < n_units; base += blockDim.x) {
+  const int n_st = M * n_chunks * 4;
+  for (int base = 0; base < n_st; base += blockDim.x) {
     const int u = base + threadIdx.x;
-    const bool live = u < n_units;
+    const bool live = u < n_st;
     const int cc = u & 3;
     const int rest = u >> 2;
     const int tok = live ? rest % M : 0, ch = live ? rest / M : 0;
@@ -375,70 +412,90 @@ __device__ __forceinline__ void run_tier(const csaq_tier& T, int cta_in_tier, in
   }
   __syncthreads();
 
-  float acc[NT][4];
+  float acc[MT][NT][4];
 #pragma unroll
-  for (int nt = 0; nt < NT; ++nt) acc[nt][0] = acc[nt][1] = acc[nt][2] = acc[nt][3] = 0.0f;
+  for (int mt = 0; mt < MT; ++mt)
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt) acc[mt][nt][0] = acc[mt][nt][1] = acc[mt][nt][2] = acc[mt][nt][3] = 0.0f;
 
-  int c_ti = 0, c_j = 0, c_slot = 0;
+  int c_j = 0, c_slot = 0, c_unit = cta_in_tier;
   for (int it = 0; it < total; ++it) {
     const int ch = warp + kWarps * c_j;
-    if constexpr (G::kDepth == 12) {
-      if (cfg.ring_div == 1) cp_async_wait<11>(); else cp_async_wait<5>();
-    } else if constexpr (G::kDepth == 8) {
+    if constexpr (I::kDepth == 8) {
       if (cfg.ring_div == 1) cp_async_wait<7>(); else cp_async_wait<3>();
-    } else if constexpr (G::kDepth == 4) {
+    } else if constexpr (I::kDepth == 4) {
       if (cfg.ring_div == 1) cp_async_wait<3>(); else cp_async_wait<1>();
     } else {
       if (cfg.ring_div == 1) cp_async_wait<1>(); else cp_async_wait<0>();
     }
     __syncwarp();
     if (ch < n_chunks) {
-      const uint8_t* slot = ring + c_slot * G::kBlockBytes;
-      uint32_t cw[2][BITS];
-#pragma unroll
-      for (int h = 0; h < 2; ++h) {
-        if constexpr (BITS == 2) {
-          const uint2 v = reinterpret_cast<const uint2*>(slot)[h * 32 + lane];
-          cw[h][0] = v.x; cw[h][1] = v.y;
-        } else {
-#pragma unroll
-          for (int q = 0; q < BITS / 4; ++q) {
-            const uint4 v = reinterpret_cast<const uint4*>(slot)[(h * (BITS / 4) + q) * 32 + lane];
-            cw[h][4 * q] = v.x; cw[h][4 * q + 1] = v.y; cw[h][4 * q + 2] = v.z; cw[h][4 * q + 3] = v.w;
-          }
-        }
-      }
-      float s0 = 1.0f, s1 = 1.0f, z0 = 0.0f, z1 = 0.0f;
-      if constexpr (BITS != 16) {
-        const float* sc = reinterpret_cast<const float*>(slot + G::kCodeBytes);
-        const uint8_t* zp = slot + G::kCodeBytes + 64;
-        s0 = sc[g]; s1 = sc[g + 8];
-        z0 = (float)zp[g]; z1 = (float)zp[g + 8];
-      }
+      const uint8_t* slot = ring + c_slot * I::kBytes;
+      // activation records of this chunk, shared by the item's tiles
       const uint2* xr = xrec + (ch * 8 * M) * 4 + c;
+      uint2 rec[NT][8];
 #pragma unroll
       for (int nt = 0; nt < NT; ++nt) {
         const int tok = nt * 8 + g;
-        uint2 rec[8];
-        if (tok < M) {
 #pragma unroll
-          for (int q = 0; q < 8; ++q) rec[q] = xr[(q * M + tok) * 4];
-        } else {
+        for (int q = 0; q < 8; ++q) rec[nt][q] = tok < M ? xr[(q * M + tok) * 4] : make_uint2(0u, 0u);
+      }
+      float2 cs[NT][2];
 #pragma unroll
-          for (int q = 0; q < 8; ++q) rec[q] = make_uint2(0u, 0u);
+      for (int nt = 0; nt < NT; ++nt) {
+        const int t0 = nt * 8 + 2 * c;
+        cs[nt][0] = (BITS != 16 && t0 < M) ? xcs[ch * M + t0] : make_float2(0.0f, 0.0f);
+        cs[nt][1] = (BITS != 16 && t0 + 1 < M) ? xcs[ch * M + t0 + 1] : make_float2(0.0f, 0.0f);
+      }
+      // codes and metadata of the item's tiles (a missing second tile reads a
+      // stale slot; its rows lie past n_rows and are never stored)
+      uint32_t cw[MT][2][BITS];
+      float sm[MT][2], zm[MT][2];
+#pragma unroll
+      for (int mt = 0; mt < MT; ++mt) {
+        const uint8_t* blk = slot + mt * G::kBlockBytes;
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          if constexpr (BITS == 2) {
+            const uint2 v = reinterpret_cast<const uint2*>(blk)[h * 32 + lane];
+            cw[mt][h][0] = v.x; cw[mt][h][1] = v.y;
+          } else {
+#pragma unroll
+            for (int q = 0; q < BITS / 4; ++q) {
+              const uint4 v = reinterpret_cast<const uint4*>(blk)[(h * (BITS / 4) + q) * 32 + lane];
+              cw[mt][h][4 * q] = v.x; cw[mt][h][4 * q + 1] = v.y; cw[mt][h][4 * q + 2] = v.z; cw[mt][h][4 * q + 3] = v.w;
+            }
+          }
         }
-        float gs[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-        chunk_mma<BITS>(cw, rec, gs);
-        if constexpr (BITS == 16) {
-          acc[nt][0] += gs[0]; acc[nt][1] += gs[1]; acc[nt][2] += gs[2]; acc[nt][3] += gs[3];
-        } else {
-          const int t0 = nt * 8 + 2 * c;
-          const float2 cs0 = t0 < M ? xcs[ch * M + t0] : make_float2(0.0f, 0.0f);
-          const float2 cs1 = t0 + 1 < M ? xcs[ch * M + t0 + 1] : make_float2(0.0f, 0.0f);
-          acc[nt][0] = fmaf(s0, fmaf(-z0, cs0.y, gs[0] - cs0.x), acc[nt][0]);
-          acc[nt][1] = fmaf(s0, fmaf(-z0, cs1.y, gs[1] - cs1.x), acc[nt][1]);
-          acc[nt][2] = fmaf(s1, fmaf(-z1, cs0.y, gs[2] - cs0.x), acc[nt][2]);
-          acc[nt][3] = fmaf(s1, fmaf(-z1, cs1.y, gs[3] - cs1.x), acc[nt][3]);
+        sm[mt][0] = sm[mt][1] = 1.0f;
+        zm[mt][0] = zm[mt][1] = 0.0f;
+        if constexpr (BITS != 16) {
+          const float* sc = reinterpret_cast<const float*>(blk + G::kCodeBytes);
+          const uint8_t* zp = blk + G::kCodeBytes + 64;
+          sm[mt][0] = sc[g]; sm[mt][1] = sc[g + 8];
+          zm[mt][0] = (float)zp[g]; zm[mt][1] = (float)zp[g + 8];
+        }
+      }
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt) {
+        float gs[MT][2][4];
+#pragma unroll
+        for (int mt = 0; mt < MT; ++mt)
+#pragma unroll
+          for (int a = 0; a < 2; ++a) gs[mt][a][0] = gs[mt][a][1] = gs[mt][a][2] = gs[mt][a][3] = 0.0f;
+        chunk_mma<BITS, MT>(cw, rec[nt], gs);
+#pragma unroll
+        for (int mt = 0; mt < MT; ++mt) {
+          const float g0 = gs[mt][0][0] + gs[mt][1][0], g1 = gs[mt][0][1] + gs[mt][1][1];
+          const float g2 = gs[mt][0][2] + gs[mt][1][2], g3 = gs[mt][0][3] + gs[mt][1][3];
+          if constexpr (BITS == 16) {
+            acc[mt][nt][0] += g0; acc[mt][nt][1] += g1; acc[mt][nt][2] += g2; acc[mt][nt][3] += g3;
+          } else {
+            acc[mt][nt][0] = fmaf(sm[mt][0], fmaf(-zm[mt][0], cs[nt][0].y, g0 - cs[nt][0].x), acc[mt][nt][0]);
+            acc[mt][nt][1] = fmaf(sm[mt][0], fmaf(-zm[mt][0], cs[nt][1].y, g1 - cs[nt][1].x), acc[mt][nt][1]);
+            acc[mt][nt][2] = fmaf(sm[mt][1], fmaf(-zm[mt][1], cs[nt][0].y, g2 - cs[nt][0].x), acc[mt][nt][2]);
+            acc[mt][nt][3] = fmaf(sm[mt][1], fmaf(-zm[mt][1], cs[nt][1].y, g3 - cs[nt][1].x), acc[mt][nt][3]);
+          }
         }
       }
     }
@@ -446,25 +503,27 @@ __device__ __forceinline__ void run_tier(const csaq_tier& T, int cta_in_tier, in
     issue();
     c_slot = (c_slot + 1 == depth) ? 0 : c_slot + 1;
 
-    if (c_j == cpw - 1) {  // end of a tile: reduce the warps' K slices
-      const int tile = cta_in_tier + c_ti * ctas_in_tier;
-      float* rw = red + warp * kTileRows * NT * 8;
+    if (c_j == cpw - 1) {  // end of a unit: reduce the warps' K slices
+      float* rw = red + warp * kRows * NT * 8;
 #pragma unroll
-      for (int nt = 0; nt < NT; ++nt) {
-        rw[g * NT * 8 + nt * 8 + 2 * c] = acc[nt][0];
-        rw[g * NT * 8 + nt * 8 + 2 * c + 1] = acc[nt][1];
-        rw[(g + 8) * NT * 8 + nt * 8 + 2 * c] = acc[nt][2];
-        rw[(g + 8) * NT * 8 + nt * 8 + 2 * c + 1] = acc[nt][3];
-        acc[nt][0] = acc[nt][1] = acc[nt][2] = acc[nt][3] = 0.0f;
-      }
+      for (int mt = 0; mt < MT; ++mt)
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) {
+          const int r0 = mt * kTileRows + g;
+          rw[r0 * NT * 8 + nt * 8 + 2 * c] = acc[mt][nt][0];
+          rw[r0 * NT * 8 + nt * 8 + 2 * c + 1] = acc[mt][nt][1];
+          rw[(r0 + 8) * NT * 8 + nt * 8 + 2 * c] = acc[mt][nt][2];
+          rw[(r0 + 8) * NT * 8 + nt * 8 + 2 * c + 1] = acc[mt][nt][3];
+          acc[mt][nt][0] = acc[mt][nt][1] = acc[mt][nt][2] = acc[mt][nt][3] = 0.0f;
+        }
       __syncthreads();
-      for (int i = threadIdx.x; i < kTileRows * NT * 8; i += blockDim.x) {
+      for (int i = threadIdx.x; i < kRows * NT * 8; i += blockDim.x) {
         const int r = i / (NT * 8), tok = i % (NT * 8);
-        const int row = tile * kTileRows + r;
+        const int row = c_unit * kRows + r;
         if (row >= T.n_rows || tok >= M) continue;
         float v = 0.0f;
 #pragma unroll
-        for (int w = 0; w < kWarps; ++w) v += red[w * kTileRows * NT * 8 + i];
+        for (int w = 0; w < kWarps; ++w) v += red[w * kRows * NT * 8 + i];
         v *= xexp[tok];
         const int orow = T.out_rows[row];
         if (T.bias) v += to_f32<ACT>(reinterpret_cast<const ACT*>(T.bias)[orow]);
@@ -473,7 +532,7 @@ __device__ __forceinline__ void run_tier(const csaq_tier& T, int cta_in_tier, in
       }
       __syncthreads();
       c_j = 0;
-      ++c_ti;
+      c_unit += ctas_in_tier;
     } else {
       ++c_j;
     }
@@ -609,8 +668,8 @@ constexpr int kSmemBudget = 227 * 1024;
 
 int ring_bytes(int div) {
   int m = 0;
-  const int r[4] = {Geo<2>::kDepth * Geo<2>::kBlockBytes, Geo<4>::kDepth * Geo<4>::kBlockBytes,
-                    Geo<8>::kDepth * Geo<8>::kBlockBytes, Geo<16>::kDepth * Geo<16>::kBlockBytes};
+  const int r[4] = {Item<2>::kDepth * Item<2>::kBytes, Item<4>::kDepth * Item<4>::kBytes,
+                    Item<8>::kDepth * Item<8>::kBytes, Item<16>::kDepth * Item<16>::kBytes};
   for (int i = 0; i < 4; ++i) m = r[i] > m ? r[i] : m;
   return kWarps * m / div;
 }
@@ -620,7 +679,7 @@ int ring_bytes(int div) {
 bool plan(int64_t K, int M, int NT, LaunchCfg& cfg) {
   cfg.x_bytes = (int)(2 * M * K);
   cfg.cs_bytes = (int)(((K / 128) * M * 8 + 15) / 16 * 16);
-  const int fixed = cfg.x_bytes + cfg.cs_bytes + 64 + kWarps * kTileRows * NT * 8 * 4;
+  const int fixed = cfg.x_bytes + cfg.cs_bytes + 64 + kWarps * 32 * NT * 8 * 4;
   for (int div = 1; div <= 2; div *= 2) {
     cfg.ring_div = div;
     cfg.smem_bytes = fixed + ring_bytes(div);
@@ -664,24 +723,27 @@ int launch_mma_block(const TierParams& TP, int64_t K, const ACT* x, int M, int64
   const int max_ctas = num_sms() * per_sm;
   KParams P;
   P.tp = TP;
-  // persistent CTAs per tier in proportion to the tier's bytes, at most one per tile
+  // persistent CTAs per tier in proportion to the tier's bytes, at most one
+  // per work unit (item_tiles tiles)
   double total_bytes = 0.0;
-  int total_tiles = 0;
+  int total_units = 0;
   for (int i = 0; i < TP.n_tiers; ++i) {
     const csaq_tier& t = TP.t[i];
     total_bytes += (double)t.n_rows * (double)block_bytes(t.bits);
-    total_tiles += (t.n_rows + kTileRows - 1) / kTileRows;
+    const int tiles = (t.n_rows + kTileRows - 1) / kTileRows;
+    total_units += (tiles + item_tiles(t.bits) - 1) / item_tiles(t.bits);
   }
-  if (total_tiles == 0) return CSAQ_OK;
-  const int budget = total_tiles < max_ctas ? total_tiles : max_ctas;
+  if (total_units == 0) return CSAQ_OK;
+  const int budget = total_units < max_ctas ? total_units : max_ctas;
   int ctas = 0;
   for (int i = 0; i < TP.n_tiers; ++i) {
     const csaq_tier& t = TP.t[i];
     const int tiles = (t.n_rows + kTileRows - 1) / kTileRows;
+    const int units = (tiles + item_tiles(t.bits) - 1) / item_tiles(t.bits);
     int n = 0;
-    if (tiles > 0) {
+    if (units > 0) {
       n = (int)((double)budget * ((double)t.n_rows * (double)block_bytes(t.bits)) / total_bytes + 0.5);
-      n = n < 1 ? 1 : (n > tiles ? tiles : n);
+      n = n < 1 ? 1 : (n > units ? units : n);
     }
     P.cta_start[i] = ctas;
     ctas += n;
