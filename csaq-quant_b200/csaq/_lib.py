@@ -75,6 +75,15 @@ _SIGNATURES = {
     "csaq_greedy_cliques": (c_int, [c_vp, c_i64, c_i64, c_vp, c_vp, c_vp]),
     "csaq_salience_accum": (c_int, [c_vp, c_vp, c_int, c_i64, c_vp, c_vp]),
     "csaq_salience_finalize": (c_int, [c_vp, c_i64, c_i64, c_vp]),
+    "csaq_rmsnorm": (c_int, [c_vp, c_i64, c_vp, c_vp, c_i64, c_i64, c_i64, ctypes.c_float, c_int, c_vp]),
+    "csaq_rope_kv": (c_int, [c_vp, c_i64, c_vp, c_i64, c_vp, c_i64, c_vp, c_i64, c_i64, c_i64, c_i64, c_i64,
+                             c_vp, c_vp, c_vp, c_vp, c_vp, c_i64, c_int, c_vp]),
+    "csaq_attention_workspace_floats": (c_i64, [c_i64, c_i64, c_i64, c_i64, c_i64, c_i64]),
+    "csaq_decode_attention": (c_int, [c_vp, c_vp, c_vp, c_vp, c_i64, c_i64, c_i64, c_i64, c_i64, c_i64,
+                                      ctypes.c_float, c_vp, c_vp, c_vp, c_int, c_vp]),
+    "csaq_silu_mul": (c_int, [c_vp, c_i64, c_vp, c_i64, c_vp, c_i64, c_i64, c_i64, c_int, c_vp]),
+    "csaq_spec_accept": (c_int, [c_vp, c_vp, c_i64, c_i64, c_vp, c_vp, c_vp, c_i64, c_vp, c_vp, c_vp, c_vp, c_vp]),
+    "csaq_greedy_commit": (c_int, [c_vp, c_i64, c_vp, c_vp, c_vp, c_i64, c_vp, c_vp, c_vp]),
 }
 
 _lib = None

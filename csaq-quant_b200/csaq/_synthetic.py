@@ -90,3 +90,68 @@ def salience_inputs(channels: int, k: int, n_samples: int, seed: int = 0,
     grads = [(torch.randn(channels, k, generator=gen) * 1e-3).to(dtype)
              for _ in range(n_samples)]
     return W, grads
+
+
+# ── decoder-shaped models (random init, no checkpoint needed) ────────────────
+DECODERS = {
+    # name: (architecture, hidden, intermediate, layers, heads, kv heads, vocab)
+    "qwen1.5-0.5b": ("qwen2", 1024, 2816, 24, 16, 16, 151936),
+    "llama3-8b": ("llama", 4096, 14336, 32, 32, 8, 128256),
+    "llama3-70b": ("llama", 8192, 28672, 80, 64, 8, 128256),
+    "tiny-llama": ("llama", 512, 1536, 2, 4, 2, 2048),
+    "tiny-qwen2": ("qwen2", 512, 1408, 2, 4, 4, 2048),
+}
+
+
+def decoder_config(name: str, n_layers: int = None):
+    """HF config of a decoder shape (head_dim 128, default rope)."""
+    from transformers import LlamaConfig, Qwen2Config
+    arch, h, inter, layers, heads, kv, vocab = DECODERS[name]
+    kw = dict(hidden_size=h, intermediate_size=inter, num_hidden_layers=n_layers or layers,
+              num_attention_heads=heads, num_key_value_heads=kv, vocab_size=vocab,
+              max_position_embeddings=4096, initializer_range=0.02, tie_word_embeddings=False)
+    return LlamaConfig(**kw) if arch == "llama" else Qwen2Config(**kw)
+
+
+def build_decoder(name: str, device="cuda", dtype: torch.dtype = torch.bfloat16, seed: int = 0,
+                  n_layers: int = None):
+    """Random-init decoder: every weight ~ N(0, 0.02^2), norms = 1, biases 0."""
+    from transformers import AutoModelForCausalLM
+    cfg = decoder_config(name, n_layers)
+    torch.manual_seed(seed)
+    with torch.device(device):
+        model = AutoModelForCausalLM.from_config(cfg, dtype=dtype)
+    gen = torch.Generator(device=device).manual_seed(seed)
+    with torch.no_grad():
+        for n, p in model.named_parameters():
+            if p.dim() >= 2:
+                p.copy_(torch.randn(p.shape, generator=gen, device=device, dtype=torch.float32) * 0.02)
+            elif "norm" in n:
+                p.fill_(1.0)
+            else:
+                p.zero_()
+    model.eval()
+    return model
+
+
+def synthetic_salience(model, seed: int = 0):
+    """Row salience sum_k |G*W| with G ~ N(0, 1e-3^2) for every quantisable
+    linear, returned as (C, K) expanded views of the per-row value / K (the
+    solver and apply_csaq only reduce over K)."""
+    import torch.nn as nn
+    out = {}
+    gen = torch.Generator(device=next(model.parameters()).device).manual_seed(seed)
+    skip = ("lm_head", "embed_tokens")
+    for name, m in model.named_modules():
+        if not isinstance(m, nn.Linear) or any(s in name for s in skip):
+            continue
+        W = m.weight.data
+        C, K = W.shape
+        rs = torch.empty(C, dtype=torch.float32, device=W.device)
+        step = max(1, (1 << 26) // K)
+        for r0 in range(0, C, step):
+            w = W[r0:r0 + step].float()
+            g = torch.randn(w.shape, generator=gen, device=W.device) * 1e-3
+            rs[r0:r0 + step] = (g * w).abs().sum(dim=1)
+        out[name] = (rs / K)[:, None].expand(C, K)
+    return out

@@ -1,0 +1,507 @@
+"""csaq.core — the three-phase pipeline on B200.
+
+Drop-in for csaq-quant's ``csaq/core.py`` (same names, arguments, return
+values): calibration profiling (salience and co-activation cliques), the
+bit-budget solver, and application of the quantised layers.
+
+Device work runs in libcsaq_b200.so:
+* forward hooks turn each linear's output into a bit-packed top-k
+  co-activation mask (csaq_act_mask) that stays on the GPU;
+* |grad * W| salience accumulates in fp32 on the GPU (csaq_salience_accum);
+* cliques come from popcount intersection counts (csaq_coact_counts), fp32
+  Jaccard threshold bits (csaq_jaccard_bits) and the seed-order greedy
+  partition (csaq_greedy_cliques).
+The solver and the layer bookkeeping are host orchestration, as in the
+reference.
+
+Layer layout: with ``config.group_size == -1`` (the default) every layer is
+the reference's uniform CSAQLinear built by ``CSAQLinear.from_cliques``;
+with ``group_size > 0`` (e.g. 128) each layer becomes a mixed-row layer whose
+rows carry the bit-width the solver gave their clique.
+"""
+
+from __future__ import annotations
+
+import time
+import warnings
+from collections import defaultdict
+from typing import Any, Dict, Iterator, List, Optional, Tuple, Union
+
+import torch
+import torch.nn as nn
+
+from . import _lib
+from ._lib import check, dtype_code, lib, ptr, stream_of
+from .config import CSAQConfig
+from .kernels import CSAQLinear, _get_submodule, inject_csaq_linear
+
+BudgetMap = Dict[str, List[Dict[str, Any]]]
+SalienceMap = Dict[str, torch.Tensor]
+CliqueMap = Dict[str, List[List[int]]]
+
+
+def _prepare_calib_data(calib_data: Union[List[Dict[str, torch.Tensor]], List[str]], model: nn.Module,
+                        device: str = "cpu", tokenizer: Any = None,
+                        seq_len: int = 128) -> List[Dict[str, torch.Tensor]]:
+    """Normalise calibration data to tokenised batches (csaq/core.py:40-89)."""
+    if not calib_data:
+        raise ValueError("[CSAQ] calib_data is empty.")
+    if isinstance(calib_data[0], dict):
+        out = []
+        for batch in calib_data:
+            if "attention_mask" not in batch:
+                batch = dict(batch)
+                batch["attention_mask"] = torch.ones_like(batch["input_ids"])
+            out.append({k: v.to(device) for k, v in batch.items()})
+        return out
+    if isinstance(calib_data[0], str):
+        if tokenizer is None:
+            raise ValueError(
+                "[CSAQ] calib_data contains raw strings but no tokenizer was provided.  Pass "
+                "tokenizer= to quantize(), or pre-tokenise your texts using "
+                "build_calibration_data() before calling quantize().")
+        batches = []
+        for text in calib_data:
+            enc = tokenizer(str(text), return_tensors="pt", max_length=seq_len, truncation=True,
+                            padding="max_length")
+            batches.append({k: v.to(device) for k, v in enc.items()})
+        return batches
+    raise TypeError("[CSAQ] Unsupported calib_data type.  Expected List[Dict] or List[str].")
+
+
+def _linear_modules(model: nn.Module) -> Iterator[Tuple[str, nn.Linear]]:
+    """Quantisable nn.Linear layers (csaq/core.py:92-102)."""
+    skip = ("lm_head", "embed_tokens", "embed_positions", "wte", "wpe")
+    for name, module in model.named_modules():
+        if not isinstance(module, nn.Linear) or module.weight is None:
+            continue
+        if any(p in name for p in skip):
+            continue
+        yield name, module
+
+
+# ─────────────────────────────────────────────────────────────────────────────
+# GPU calibration primitives
+# ─────────────────────────────────────────────────────────────────────────────
+
+class MaskHistory:
+    """Bit-packed co-activation masks of one layer, channel-major, on the GPU.
+
+    Grows by doubling; bit t of channel c is token t of the calibration run.
+    """
+
+    def __init__(self, channels: int, device: torch.device, capacity_tokens: int = 4096):
+        self.C = channels
+        self.dev = device
+        self.n_tok = 0
+        self.words = max(1, (capacity_tokens + 31) // 32)
+        self.bits = torch.zeros(channels, self.words, dtype=torch.int32, device=device)
+        self.tok_thr = torch.zeros(1, dtype=torch.int32, device=device)
+
+    def _reserve(self, n_tok: int) -> None:
+        need = (self.n_tok + n_tok + 31) // 32 + 1
+        if need <= self.words:
+            return
+        words = max(need, 2 * self.words)
+        nb = torch.zeros(self.C, words, dtype=torch.int32, device=self.dev)
+        nb[:, : self.words] = self.bits
+        self.bits, self.words = nb, words
+
+    def append(self, act: torch.Tensor, mode: int, thr: float = 0.0, k: int = 1) -> None:
+        a = act.detach().reshape(-1, act.shape[-1])
+        if not a.is_cuda:
+            a = a.to(self.dev)
+        if a.dtype not in (torch.float32, torch.float16, torch.bfloat16):
+            a = a.float()
+        if a.stride(1) != 1:
+            a = a.contiguous()
+        n = a.shape[0]
+        if n == 0:
+            return
+        # keep every append on a 32-token boundary: pad the running count
+        self.n_tok = (self.n_tok + 31) // 32 * 32 if self.n_tok % 32 else self.n_tok
+        self._reserve(n)
+        if mode == 1 and self.tok_thr.numel() < n:
+            self.tok_thr = torch.zeros(n, dtype=torch.int32, device=self.dev)
+        check(lib().csaq_act_mask(a.data_ptr(), dtype_code(a.dtype), n, self.C, a.stride(0), mode,
+                                  float(thr), int(k), self.tok_thr.data_ptr(), self.bits.data_ptr(),
+                                  self.words, self.n_tok, stream_of(a)), "act_mask")
+        self.n_tok += n
+
+    def words_used(self) -> int:
+        return (self.n_tok + 31) // 32
+
+
+def coactivation_counts(bits: torch.Tensor, n_words: int) -> Tuple[torch.Tensor, torch.Tensor]:
+    """Exact intersection counts I (C, C) int32 and activation counts f (C,) int32."""
+    C = bits.shape[0]
+    inter = torch.empty(C, C, dtype=torch.int32, device=bits.device)
+    f = torch.empty(C, dtype=torch.int32, device=bits.device)
+    check(lib().csaq_coact_counts(bits.data_ptr(), C, n_words, bits.stride(0), inter.data_ptr(), C,
+                                  f.data_ptr(), stream_of(bits)), "coact_counts")
+    return inter, f
+
+
+def jaccard_cliques(inter: torch.Tensor, f: torch.Tensor, threshold: float) -> List[List[int]]:
+    """Seed-order greedy cliques over Jaccard >= threshold (csaq/core.py:263-285)."""
+    C = inter.shape[0]
+    words = (C + 31) // 32
+    adj = torch.empty(C, words, dtype=torch.int32, device=inter.device)
+    thr32 = float(torch.tensor(threshold, dtype=torch.float32))
+    st = stream_of(inter)
+    check(lib().csaq_jaccard_bits(inter.data_ptr(), inter.stride(0), f.data_ptr(), C, thr32,
+                                  adj.data_ptr(), words, st), "jaccard_bits")
+    labels = torch.empty(C, dtype=torch.int32, device=inter.device)
+    n = torch.zeros(1, dtype=torch.int32, device=inter.device)
+    check(lib().csaq_greedy_cliques(adj.data_ptr(), words, C, labels.data_ptr(), n.data_ptr(), st),
+          "greedy_cliques")
+    return cliques_from_labels(labels)
+
+
+def cliques_from_labels(labels: torch.Tensor) -> List[List[int]]:
+    """Clique lists (ascending members, seed first) from per-channel labels."""
+    lab = labels.to(torch.int64).cpu()
+    order = torch.argsort(lab, stable=True)
+    counts = torch.bincount(lab)
+    return [g.tolist() for g in torch.split(order, counts.tolist())]
+
+
+def salience_accumulate(acc: torch.Tensor, grad: torch.Tensor, weight: torch.Tensor) -> None:
+    """acc += |grad * weight| in fp32 (csaq/core.py:204-210)."""
+    g = grad.contiguous()
+    w = weight.contiguous()
+    if g.dtype != w.dtype:
+        g = g.to(w.dtype)
+    if w.dtype not in (torch.float32, torch.float16, torch.bfloat16):
+        g, w = g.float(), w.float()
+    check(lib().csaq_salience_accum(g.data_ptr(), w.data_ptr(), dtype_code(w.dtype), w.numel(),
+                                    acc.data_ptr(), stream_of(acc)), "salience_accum")
+
+
+# ─────────────────────────────────────────────────────────────────────────────
+# Phase 1 & 2: CausalProfiler (csaq/core.py:109-287)
+# ─────────────────────────────────────────────────────────────────────────────
+
+class CausalProfiler:
+    """Causal salience (|dL/dw * w|) and Jaccard co-activation cliques.
+
+    Same interface as csaq/core.py:109-287. Masks and salience accumulators
+    live on the GPU of each layer; the Spearman early stop follows
+    csaq/core.py:212-230.
+    """
+
+    _EARLY_STOP_RHO: float = 0.99
+    _EARLY_STOP_MIN_BATCHES: int = 16
+    _EVAL_STRIDE: int = 8
+    _SPEARMAN_SAMPLE: int = 50_000
+
+    def __init__(self, model: nn.Module, config: CSAQConfig) -> None:
+        self.model = model
+        self.config = config
+        self.salience: SalienceMap = {}
+        self._masks: Dict[str, MaskHistory] = {}
+        self._hooks: List[Any] = []
+        self._modules: Dict[str, nn.Linear] = {}
+        dev = _lib.cuda_device()
+        for name, module in _linear_modules(model):
+            self._modules[name] = module
+            mdev = module.weight.device if module.weight.is_cuda else dev
+            self.salience[name] = torch.zeros(module.weight.shape, dtype=torch.float32, device=mdev)
+            self._masks[name] = MaskHistory(module.weight.shape[0], mdev)
+            self._register_hook(name, module)
+
+    def _register_hook(self, name: str, module: nn.Linear) -> None:
+        alpha = self.config.salience_alpha
+
+        def forward_hook(m: nn.Module, inp, out: torch.Tensor) -> None:
+            with torch.no_grad():
+                C = out.shape[-1]
+                frac = min(1.0, 0.1 * alpha)
+                k = max(1, int(frac * C))
+                self._masks[name].append(out, mode=1, k=k)
+
+        self._hooks.append(module.register_forward_hook(forward_hook))
+
+    def add_activation_masks(self, name: str, act: torch.Tensor, threshold: Optional[float] = None) -> None:
+        """Append co-activation masks from activations directly: act > threshold
+        when given (in act's dtype), else the hook's top-k rule."""
+        mh = self._masks[name]
+        if threshold is None:
+            k = max(1, int(min(1.0, 0.1 * self.config.salience_alpha) * act.shape[-1]))
+            mh.append(act, mode=1, k=k)
+        else:
+            thr = float(torch.tensor(threshold, dtype=act.dtype)) if act.is_floating_point() else threshold
+            mh.append(act, mode=0, thr=thr)
+
+    def profile(self, calib_data: List[Dict[str, torch.Tensor]],
+                verbose: bool = True) -> Tuple[SalienceMap, CliqueMap]:
+        self.model.train()
+        n_samples = len(calib_data)
+        actual_batches = 0
+        prev_ranks = None
+        eval_idx = None
+        first_device = next(self.model.parameters()).device
+        for i, batch in enumerate(calib_data):
+            actual_batches += 1
+            batch = {k: v.to(first_device) if isinstance(v, torch.Tensor) else v for k, v in batch.items()}
+            labels = batch.get("labels", batch.get("input_ids"))
+            try:
+                out = self.model(**batch, labels=labels)
+                out.loss.backward()
+            except Exception as exc:  # the reference skips a failing batch (csaq/core.py:199-202)
+                warnings.warn(f"[CSAQ] Skipping calibration batch {i}: {exc}")
+                self.model.zero_grad()
+                continue
+            with torch.no_grad():
+                for name, module in self._modules.items():
+                    if module.weight.grad is not None:
+                        acc = self.salience[name]
+                        g, w = module.weight.grad, module.weight.data
+                        if not g.is_cuda:
+                            g, w = g.to(acc.device), w.to(acc.device)
+                        salience_accumulate(acc, g, w)
+            self.model.zero_grad()
+            if (i + 1) % self._EVAL_STRIDE == 0 and (i + 1) >= self._EARLY_STOP_MIN_BATCHES:
+                all_s = torch.cat([self.salience[n].flatten().to(first_device) for n in self._modules])
+                if eval_idx is None:
+                    size = min(self._SPEARMAN_SAMPLE, all_s.numel())
+                    eval_idx = torch.randperm(all_s.numel(), device=all_s.device)[:size]
+                ranks = all_s[eval_idx].argsort().argsort().float()
+                if prev_ranks is not None:
+                    n_r = float(ranks.numel())
+                    d = ranks - prev_ranks
+                    rho = 1.0 - (6.0 * (d ** 2).sum().item()) / (n_r * (n_r ** 2 - 1))
+                    if rho >= self._EARLY_STOP_RHO:
+                        if verbose:
+                            print(f"[CSAQ] Early stop at batch {i + 1}/{n_samples} (ρ={rho:.4f})")
+                        break
+                prev_ranks = ranks.clone()
+        for name in self.salience:
+            acc = self.salience[name]
+            check(lib().csaq_salience_finalize(acc.data_ptr(), acc.numel(), max(actual_batches, 1),
+                                               stream_of(acc)), "salience_finalize")
+        for h in self._hooks:
+            h.remove()
+        self.model.eval()
+        return self.salience, self._build_cliques()
+
+    def _build_cliques(self) -> CliqueMap:
+        """Partition each layer's output channels (csaq/core.py:240-287)."""
+        if self.config.clique_mode == "per_channel":
+            return {name: [[i] for i in range(m.weight.shape[0])] for name, m in self._modules.items()}
+        out: CliqueMap = {}
+        for name, module in self._modules.items():
+            mh = self._masks[name]
+            C = module.weight.shape[0]
+            if mh.n_tok == 0:
+                out[name] = [[i] for i in range(C)]
+                continue
+            inter, f = coactivation_counts(mh.bits, mh.words_used())
+            out[name] = jaccard_cliques(inter, f, self.config.clique_threshold)
+            del inter
+            self._masks[name] = MaskHistory(C, mh.dev)
+        return out
+
+
+# ─────────────────────────────────────────────────────────────────────────────
+# Phase 3: solver (csaq/core.py:294-361)
+# ─────────────────────────────────────────────────────────────────────────────
+
+def solve_clique_budget(salience: SalienceMap, cliques: CliqueMap,
+                        config: CSAQConfig) -> Tuple[BudgetMap, Dict[str, int], float]:
+    """Assign bit-widths to cliques to hit config.target_bits on average.
+
+    Same greedy as csaq/core.py:294-361: cliques start at the lowest option,
+    are ordered by salience density (stable, descending), the top
+    max(1, floor(protection_floor * n)) are lifted to >= 8 bits when 8 is an
+    option, then each clique in order takes upgrades while the running total
+    stays within target_bits * elements. Per-clique sums are taken on the
+    device in one pass per layer.
+    """
+    options = sorted(config.bit_options)
+    min_bits = options[0]
+    recs = []  # (layer, rows, salience, elems, leader)
+    for name, layer_cliques in cliques.items():
+        s = salience[name]
+        if not layer_cliques:
+            continue
+        if s.dtype != torch.float32:
+            s = s.float()
+        C, K = s.shape
+        row_sal = s.sum(dim=1)
+        lab = torch.empty(C, dtype=torch.int64)
+        flat, starts = [], []
+        for ci, c in enumerate(layer_cliques):
+            starts.append(len(flat))
+            flat.extend(c)
+        idx = torch.tensor(flat, dtype=torch.int64, device=s.device)
+        seg = torch.repeat_interleave(torch.arange(len(layer_cliques), device=s.device),
+                                      torch.tensor([len(c) for c in layer_cliques], device=s.device))
+        rs = row_sal[idx]
+        c_sal = torch.zeros(len(layer_cliques), dtype=torch.float32, device=s.device).index_add_(0, seg, rs)
+        # leader: first row of maximal row salience inside the clique
+        big = torch.full((len(layer_cliques),), -float("inf"), dtype=torch.float32, device=s.device)
+        big = big.scatter_reduce(0, seg, rs, reduce="amax")
+        is_max = rs == big[seg]
+        pos_in = torch.arange(idx.numel(), device=s.device)
+        first = torch.full((len(layer_cliques),), idx.numel(), dtype=torch.int64, device=s.device)
+        first = first.scatter_reduce(0, seg, torch.where(is_max, pos_in, torch.full_like(pos_in, idx.numel())),
+                                     reduce="amin")
+        leaders = idx[first.clamp(max=idx.numel() - 1)].cpu().tolist()
+        c_sal = c_sal.cpu().tolist()
+        for ci, c in enumerate(layer_cliques):
+            recs.append((name, c, float(c_sal[ci]), len(c) * K, int(leaders[ci])))
+    if not recs:
+        return {}, {}, float(config.target_bits)
+    total = sum(r[3] for r in recs)
+    bits = [min_bits] * len(recs)
+    current = sum(r[3] * min_bits for r in recs)
+    target_total = config.target_bits * total
+    order = sorted(range(len(recs)), key=lambda i: recs[i][2] / max(recs[i][3], 1), reverse=True)
+    n_protect = max(1, int(config.protection_floor * len(recs)))
+    floor_target = min(8, max(options))
+    for i in order[:n_protect]:
+        fb = max(bits[i], floor_target)
+        if fb > bits[i] and fb in options:
+            current += (fb - bits[i]) * recs[i][3]
+            bits[i] = fb
+    for i in order:
+        for b in options:
+            if b <= bits[i]:
+                continue
+            cost = (b - bits[i]) * recs[i][3]
+            if current + cost <= target_total:
+                current += cost
+                bits[i] = b
+            else:
+                break
+    budget: BudgetMap = defaultdict(list)
+    stats: Dict[str, int] = defaultdict(int)
+    for i in order:
+        name, rows, sal, elems, leader = recs[i]
+        budget[name].append({"layer": name, "rows": rows, "salience": sal, "elems": elems,
+                             "bits": bits[i], "leader": leader})
+        stats[f"int{bits[i]}"] += elems
+    return dict(budget), dict(stats), current / max(total, 1)
+
+
+# ─────────────────────────────────────────────────────────────────────────────
+# Phase 3b: apply (csaq/core.py:368-418)
+# ─────────────────────────────────────────────────────────────────────────────
+
+def _protect_rows(salience_rows: torch.Tensor, floor: float) -> torch.Tensor:
+    n = salience_rows.shape[0]
+    n_protect = max(1, int(floor * n))
+    return salience_rows.topk(n_protect).indices.sort().values
+
+
+def apply_csaq(model: nn.Module, budget: BudgetMap, salience: SalienceMap, config: CSAQConfig,
+               verbose: bool = True) -> Dict[str, List[int]]:
+    """Replace linears by CSAQLinear and register the verify-pass rows.
+
+    Uniform layers (group_size -1) follow csaq/core.py:368-418 exactly,
+    except that the fp16 copies of the protected rows hold the original
+    weights (the reference copies the dequantised rows, which makes its
+    verify pass equal to its draft pass). Mixed layers (group_size > 0) give
+    each row its clique's bit-width.
+    """
+    causal_map: Dict[str, List[int]] = {}
+    mixed = config.group_size is not None and config.group_size > 0
+    originals: Dict[str, torch.Tensor] = {}
+    for name in budget:
+        mod = _get_submodule(model, name)
+        if isinstance(mod, nn.Linear) and name in salience:
+            row_sal = salience[name].float().sum(dim=1)
+            top = _protect_rows(row_sal, config.protection_floor)
+            originals[name] = mod.weight.data[top.to(mod.weight.device)].to(torch.float16).clone()
+    if mixed:
+        replaced = 0
+        for name, clique_list in budget.items():
+            parent_name, _, child_name = name.rpartition(".")
+            parent = model if not parent_name else _get_submodule(model, parent_name)
+            child = getattr(parent, child_name, None) if parent is not None else None
+            if not isinstance(child, nn.Linear):
+                continue
+            tier_rows: Dict[int, List[int]] = defaultdict(list)
+            for c in clique_list:
+                tier_rows[int(c["bits"])].extend(c["rows"])
+            covered = set(r for rows in tier_rows.values() for r in rows)
+            missing = [r for r in range(child.out_features) if r not in covered]
+            if missing:
+                tier_rows[max(config.bit_options)].extend(missing)
+            tr = {b: torch.tensor(sorted(set(r)), dtype=torch.int64) for b, r in tier_rows.items()}
+            prot = None
+            if name in salience:
+                prot = _protect_rows(salience[name].float().sum(dim=1), config.protection_floor)
+            layer = CSAQLinear.from_tiers(child, tr, group_size=config.group_size, protected_rows=prot)
+            setattr(parent, child_name, layer)
+            replaced += 1
+        if verbose:
+            print(f"[CSAQ] Replaced {replaced} nn.Linear layers with mixed-row CSAQLinear.")
+    else:
+        inject_csaq_linear(model, budget, verbose=verbose)
+    for mod_name in budget:
+        module = _get_submodule(model, mod_name)
+        if not isinstance(module, CSAQLinear) or mod_name not in salience:
+            continue
+        top = _protect_rows(salience[mod_name].float().sum(dim=1), config.protection_floor)
+        if not mixed:
+            module.set_protected_rows(top.to(module._buf_device()), originals[mod_name])
+        causal_map[mod_name] = top.tolist()
+    if verbose:
+        n_protected = sum(len(v) for v in causal_map.values())
+        print(f"[CSAQ] Protected {n_protected} rows across {len(causal_map)} layers for speculative decoding.")
+    return causal_map
+
+
+def quantize(model: nn.Module, calib_data, config: Optional[CSAQConfig] = None, verbose: bool = True,
+             tokenizer: Any = None, seq_len: int = 128,
+             calibration_domain: str = "user_provided") -> Tuple[nn.Module, Dict[str, Any]]:
+    """Full pipeline (csaq/core.py:425-553): profile -> solve -> apply."""
+    if config is None:
+        config = CSAQConfig()
+    t0 = time.time()
+    if verbose:
+        print(f"\n{'=' * 60}\n  CSAQ Quantization Pipeline (B200)\n  Target       : {config.target_bits} "
+              f"bits/weight\n  Bit options  : {config.bit_options}\n  Clique thresh: "
+              f"{config.clique_threshold}\n  Domain       : {calibration_domain}\n{'=' * 60}\n")
+    if getattr(getattr(model, "config", None), "tie_word_embeddings", False):
+        warnings.warn("[CSAQ] tie_word_embeddings=True detected. Untying for safe quantisation.",
+                      stacklevel=2)
+        model.config.tie_word_embeddings = False
+        try:
+            if model.get_input_embeddings().weight is model.get_output_embeddings().weight:
+                model.get_output_embeddings().weight = nn.Parameter(
+                    model.get_output_embeddings().weight.detach().clone().contiguous())
+        except Exception:
+            pass
+    device = next(model.parameters()).device
+    calib = _prepare_calib_data(calib_data, model, str(device), tokenizer=tokenizer, seq_len=seq_len)
+
+    def _mem():
+        if torch.cuda.is_available():
+            torch.cuda.synchronize()
+            return torch.cuda.memory_allocated() / 1024 ** 3
+        import os
+        import psutil
+        return psutil.Process(os.getpid()).memory_info().rss / 1024 ** 3
+
+    mem_before = _mem()
+    profiler = CausalProfiler(model, config)
+    salience, cliques = profiler.profile(calib, verbose=verbose)
+    cliques_count = sum(len(v) for v in cliques.values())
+    budget, tier_stats, actual_bits = solve_clique_budget(salience, cliques, config)
+    if verbose:
+        print(f"[CSAQ] Actual avg bits: {actual_bits:.3f} (target: {config.target_bits})")
+    causal_map = apply_csaq(model, budget, salience, config, verbose=verbose)
+    mem_after = _mem()
+    saved = max(0, mem_before - mem_after)
+    pct = max(0, (mem_before - mem_after) / max(mem_before, 1e-6)) * 100
+    elapsed = time.time() - t0
+    return model, {
+        "tier_stats": tier_stats, "budget": budget, "causal_map": causal_map,
+        "actual_bits": actual_bits, "cliques_count": cliques_count, "elapsed_s": elapsed,
+        "calibration_domain": calibration_domain, "memory_before_gb": round(mem_before, 3),
+        "memory_after_gb": round(mem_after, 3), "memory_saved_gb": round(saved, 3),
+        "memory_saved_pct": round(pct, 1),
+    }

@@ -188,6 +188,53 @@ int csaq_salience_accum(const void* G, const void* W, int dtype, int64_t n, floa
                         void* stream);
 int csaq_salience_finalize(float* acc, int64_t n, int64_t n_batches, void* stream);
 
+/* ── Decoder runtime (Llama / Qwen2 decode around the quantised linears) ─── */
+/* Token (b, s) of a step with S tokens per sequence is row b*S+s of every
+ * activation matrix and sits at position pos0[b] + s. KV caches are
+ * (B, Hkv, Lmax, D). These replace the HF module forwards that
+ * CSAQInferenceEngine drives (csaq/inference.py:443-476). */
+
+/* HF RMSNorm: y = w * dtype(x * rsqrt(mean(x^2) + eps)). */
+int csaq_rmsnorm(const void* x, int64_t ldx, const void* w, void* y, int64_t ldy, int64_t M,
+                 int64_t H, float eps, int dtype, void* stream);
+
+/* Rotary embedding (rotate_half convention, cos/sin tables (Lmax, D) fp32)
+ * of q and k; writes q_out (M, Hq, D) and k/v into the caches. */
+int csaq_rope_kv(const void* q, int64_t ldq, const void* k, int64_t ldk, const void* v, int64_t ldv,
+                 const int32_t* pos0, int64_t B, int64_t S, int64_t Hq, int64_t Hkv, int64_t D,
+                 const float* cos_t, const float* sin_t, void* q_out, void* k_cache, void* v_cache,
+                 int64_t Lmax, int dtype, void* stream);
+
+/* Causal GQA decode attention of the step's S tokens against the cache
+ * (keys 0..pos0[b]+s for token s), split over 64-key chunks; the last CTA of
+ * a KV head merges the chunks. part: csaq_attention_workspace_floats floats;
+ * tickets: B*Hkv int32, zero before the first call (calls leave them zero).
+ * D must be 128. */
+int64_t csaq_attention_workspace_floats(int64_t B, int64_t S, int64_t Hq, int64_t Hkv, int64_t D,
+                                        int64_t Lmax);
+int csaq_decode_attention(const void* q, const void* k_cache, const void* v_cache,
+                          const int32_t* pos0, int64_t B, int64_t S, int64_t Hq, int64_t Hkv,
+                          int64_t D, int64_t Lmax, float scale, float* part, int32_t* tickets,
+                          void* out, int dtype, void* stream);
+
+/* HF LlamaMLP gate: h = dtype(silu(g)) * u. */
+int csaq_silu_mul(const void* g, int64_t ldg, const void* u, int64_t ldu, void* h, int64_t ldh,
+                  int64_t M, int64_t N, int dtype, void* stream);
+
+/* Greedy acceptance of one self-speculative block on the device: the fixed
+ * form of csaq/inference.py:482-549 (draft token k is compared with the
+ * verifier's prediction at position k, and the verifier's token after the
+ * accepted prefix is appended). */
+int csaq_spec_accept(const int64_t* draft, const int64_t* verify_argmax, int64_t B, int64_t K,
+                     int32_t* pos0, int64_t* out_tokens, int32_t* n_out, int64_t cap,
+                     int64_t* next_tok, int32_t* n_new, int64_t* stats, int32_t* remaining,
+                     void* stream);
+
+/* Bookkeeping of one plain greedy decode step. */
+int csaq_greedy_commit(const int64_t* tok, int64_t B, int32_t* pos0, int64_t* out_tokens,
+                       int32_t* n_out, int64_t cap, int64_t* next_tok, int32_t* remaining,
+                       void* stream);
+
 #ifdef __cplusplus
 }
 #endif
