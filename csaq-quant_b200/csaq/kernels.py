@@ -680,9 +680,7 @@ class CSAQLinear(nn.Module):
         y = torch.empty(M, N, dtype=x2.dtype, device=x2.device)
         if M:
             descs = self.gemv_descriptors(y, verify=self.verify_mode)
-            arr = _lib.tier_array(descs)
-            check(lib().csaq_qgemv(arr, len(descs), K, x2.data_ptr(), dtype_code(x2.dtype), M,
-                                   x2.stride(0), stream_of(x2)), "qgemv")
+            _lib.qgemv(descs, K, x2, M)
         y = y.view(*x.shape[:-1], N)
         return y if y.device == dev else y.to(dev)
 

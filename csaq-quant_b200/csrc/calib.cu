@@ -40,9 +40,7 @@ __global__ void mask_kernel(const T* __restrict__ act, int64_t n_tok, int64_t C,
     if (mode == 0) {
       on = to_f32<T>(v) > thr;
     } else {
-      uint32_t mag;
-      if constexpr (sizeof(T) == 2) mag = (uint32_t)(*reinterpret_cast<const uint16_t*>(&v)) & 0x7FFFu;
-      else mag = (*reinterpret_cast<const uint32_t*>(&v)) & 0x7FFFFFFFu;
+      const uint32_t mag = bits_of<T>(v) & (sizeof(T) == 2 ? 0x7FFFu : 0x7FFFFFFFu);
       on = mag >= tok_thr[t];
     }
     word |= (uint32_t)on << b;
@@ -67,9 +65,7 @@ __global__ void topk_threshold_kernel(const T* __restrict__ out, int64_t C, int6
     const uint32_t hi_mask = (shift + 8 >= 32) ? 0u : (0xFFFFFFFFu << (shift + 8));
     for (int64_t c = threadIdx.x; c < C; c += blockDim.x) {
       const T v = row[c];
-      uint32_t mag;
-      if constexpr (sizeof(T) == 2) mag = (uint32_t)(*reinterpret_cast<const uint16_t*>(&v)) & 0x7FFFu;
-      else mag = (*reinterpret_cast<const uint32_t*>(&v)) & 0x7FFFFFFFu;
+      const uint32_t mag = bits_of<T>(v) & (sizeof(T) == 2 ? 0x7FFFu : 0x7FFFFFFFu);
       if ((mag & hi_mask) == prefix) atomicAdd(&hist[(mag >> shift) & 0xFF], 1u);
     }
     __syncthreads();

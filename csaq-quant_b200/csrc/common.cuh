@@ -57,6 +57,15 @@ template <> __device__ __forceinline__ float to_f32<__nv_bfloat16>(__nv_bfloat16
   return __bfloat162float(v);
 }
 
+// Bit pattern of a value (the intrinsics, not pointer casts, which the
+// compiler may not honour for the 16-bit classes).
+template <typename T> __device__ __forceinline__ uint32_t bits_of(T v);
+template <> __device__ __forceinline__ uint32_t bits_of<float>(float v) { return __float_as_uint(v); }
+template <> __device__ __forceinline__ uint32_t bits_of<__half>(__half v) { return __half_as_ushort(v); }
+template <> __device__ __forceinline__ uint32_t bits_of<__nv_bfloat16>(__nv_bfloat16 v) {
+  return __bfloat16_as_ushort(v);
+}
+
 template <typename T> __device__ __forceinline__ T from_f32(float v);
 template <> __device__ __forceinline__ float from_f32<float>(float v) { return v; }
 template <> __device__ __forceinline__ __half from_f32<__half>(float v) { return __float2half_rn(v); }

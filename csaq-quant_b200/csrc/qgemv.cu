@@ -1,37 +1,53 @@
 // Mixed-precision quantised linear for decode / verify (small M).
 //
-// Two kernels share the csaq_tier descriptor:
+// Two kernels share the csaq_tier descriptor.
 //
-// Tensor-core kernel (qgemv_mma_kernel), reading the GEMV block layout:
-//   * A tier is repacked once (csaq_repack_tiles) into contiguous blocks, one
-//     per (16-row tile, 128-column chunk): the codes of rows g and g+8 that
-//     MMA lane (g, c) = (lane / 4, lane % 4) consumes (columns c*32..c*32+31),
-//     stored lane by lane, then the 16 rows' scales and zero points.
-//   * Persistent CTAs (8 warps), each serving tiles of one tier. The warps of a
-//     CTA split a tile's chunks; each warp streams its blocks through a
-//     cp.async ring in shared memory (several KB in flight per warp), and the
-//     warps reduce their K slices through shared memory at the tile's end.
+// Tensor-core kernel (qgemv_mma_kernel), reading the GEMV block layout
+// (csaq_repack_tiles):
+//   * A tier is cut into units of MT 16-row tiles (MT = 2 for 2/4-bit rows,
+//     1 for 8/16-bit) and 128-column chunks. The block of one (unit, chunk) is
+//     contiguous and holds, tile by tile, the codes that MMA lane
+//     (g, c) = (lane / 4, lane % 4) consumes for rows g and g+8 and columns
+//     c*32 .. c*32+31, followed by the tile's 16 fp32 scales and 16 uint8 zero
+//     points. 8-bit rows are stored as two 4-bit planes (low and high nibbles);
+//     fp16 rows are stored pre-arranged in the 4-bit column order (values in
+//     "high" positions times 16, exact).
+//   * Work = (unit, chunk) items of every tier of the launch, spread over the
+//     warps of a one-CTA-per-SM grid as contiguous ranges of equal byte cost
+//     (stream-K). Each warp streams its blocks through a cp.async ring in
+//     shared memory. A unit whose chunks all fall in one warp's range is
+//     finished in registers; a unit cut by a range boundary gets one partial
+//     sum per warp in the workspace and a ticket, and the warp completing it
+//     adds the partials in warp order. The partition depends only on the tier
+//     shapes and the SM count, so a token's result is bitwise independent of
+//     how many tokens share the launch.
 //   * Activations are staged once per CTA as fp16 MMA B-fragments ("records"),
 //     scaled per token by a power of two (exact for bf16 / fp16 inputs).
-//   * Codes become fp16 MMA operands with one LOP3 per register: OR-ing a
-//     nibble into the mantissa of 1024.0 gives 1024 + f*q with f = 1, 4, 16
-//     or 64 set by the nibble's bit position; the matching B entry is x / f,
-//     so each product is (1024 / f + q) * x. Per (chunk, token) the staging
-//     pass stores C = sum_k (1024 / f_k) x_k and S = sum_k x_k, and the chunk
-//     adds s * (g - C - zp * S) to the row, with g the fp32 MMA sum.
+//   * Codes become fp16 MMA operands with one LOP3 per register: a nibble
+//     OR-ed into the mantissa of 1024.0 gives 1024 + f*q (f = 1 or 16 by the
+//     nibble's position; 2-bit codes: 1, 4, 16, 64); the matching record entry
+//     is x / f, so each product is (1024 / f + q) * x. Per (chunk, token) the
+//     staging pass stores C = sum_k (1024 / f_k) x_k and S = sum_k x_k; a
+//     chunk adds s * (g - C - zp * S) to a row (8-bit:
+//     s * ((g_lo - C) + 16 (g_hi - C) - zp * S)), g being the MMA sum.
 //
 // CUDA-core kernel (qgemv_simt_kernel), reading the reference layout: one warp
 // per (row, 8-token block), exact fp32 (q - zp) * s per element; any K, any
 // group size, fp32 activations too.
+
+#include <algorithm>
+#include <mutex>
+#include <vector>
 
 #include "common.cuh"
 
 namespace csaq {
 namespace {
 
-constexpr int kWarps = 8;
+constexpr int kWarps = 16;  // one CTA per SM
 constexpr int kThreads = kWarps * 32;
 constexpr int kTileRows = 16;
+constexpr int kRecStride = 288;  // bytes per (chunk, token) record block: 256 + 32 (bank spread)
 
 struct TierParams {
   csaq_tier t[CSAQ_MAX_TIERS];
@@ -45,12 +61,6 @@ __device__ __forceinline__ uint4 ld_cached_v4(const void* p) {
   asm volatile("ld.global.nc.v4.u32 {%0,%1,%2,%3}, [%4];"
                : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "l"(p));
   return v;
-}
-
-__device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
-  uint32_t r;
-  asm("prmt.b32 %0, %1, %2, %3;" : "=r"(r) : "r"(a), "r"(b), "r"(sel));
-  return r;
 }
 
 __device__ __forceinline__ uint32_t lop_and_or(uint32_t a, uint32_t mask, uint32_t magic) {
@@ -71,76 +81,96 @@ __device__ __forceinline__ void mma_f16(float (&d)[4], uint32_t a0, uint32_t a1,
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }
-__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src));
-}
-__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;"); }
-template <int N> __device__ __forceinline__ void cp_async_wait() {
-  asm volatile("cp.async.wait_group %0;" ::"n"(N));
-}
-
 __device__ __forceinline__ uint32_t pack_h2(float a, float b) {
-  const __half2 h = __floats2half2_rn(a, b);
-  return *reinterpret_cast<const uint32_t*>(&h);
+  return bits_of<__half>(__float2half_rn(a)) | (bits_of<__half>(__float2half_rn(b)) << 16);
 }
 
 // ── block geometry ──────────────────────────────────────────────────────────
-// Block of one (tile, chunk): codes of 16 rows x 128 columns ordered
-// [h (row g or g+8)][q (16-byte piece of the lane's columns)][lane][16 B]
-// (2-bit: [h][lane][8 B]), then 16 fp32 scales and 16 uint8 zero points.
-template <int BITS> struct Geo {
-  static constexpr int kLaneBytes = 4 * BITS;               // per row, per lane
-  static constexpr int kCodeBytes = 16 * 16 * BITS;         // 16 rows x 128 columns
-  static constexpr int kMetaBytes = BITS == 16 ? 0 : 80;
-  static constexpr int kBlockBytes = (kCodeBytes + kMetaBytes + 15) / 16 * 16;
-};
-
-__host__ __device__ __forceinline__ int block_bytes(int bits) {
-  switch (bits) {
-    case 2: return Geo<2>::kBlockBytes;
-    case 4: return Geo<4>::kBlockBytes;
-    case 8: return Geo<8>::kBlockBytes;
-    default: return Geo<16>::kBlockBytes;
-  }
+__host__ __device__ __forceinline__ int unit_tiles(int bits) { return (bits == 2 || bits == 4) ? 2 : 1; }
+__host__ __device__ __forceinline__ int code_bytes(int bits) {  // one tile x one chunk
+  return bits == 2 ? 512 : bits == 4 ? 1024 : bits == 8 ? 2048 : 4096;
+}
+__host__ __device__ __forceinline__ int tile_block_bytes(int bits) {
+  return bits == 16 ? 4096 : (code_bytes(bits) + 80 + 15) / 16 * 16;
+}
+__host__ __device__ __forceinline__ int chunk_bytes(int bits) {  // one unit x one chunk
+  return unit_tiles(bits) * tile_block_bytes(bits);
 }
 
 // ── repack: reference layout -> GEMV blocks ─────────────────────────────────
-// One thread per 16-byte (2-bit: 8-byte) code piece or per metadata entry.
-__global__ void repack_codes_kernel(const csaq_tier T, int64_t n_chunks, int bits, int64_t n_tiles,
+// Block of (unit, chunk) at ((unit * n_chunks) + chunk) * chunk_bytes; inside,
+// tile mt at mt * tile_block_bytes. Code pieces (16 B; 2-bit: 8 B) of a tile:
+//   4-bit : [h][lane]         bytes of row g+8h, columns c*32..+32 (reference nibbles)
+//   8-bit : [plane][h][lane]  nibble plane p (q >> 4p) & 15 of those columns
+//   16-bit: [h][q][lane]      fp16 of columns c*32+8q..+8 as (w0,w4),(16w1,16w5),(w2,w6),(16w3,16w7)
+//   2-bit : [h][lane]         reference bytes (8 B = 32 codes)
+__global__ void repack_codes_kernel(const csaq_tier T, int64_t n_chunks, int64_t n_units,
                                     uint8_t* __restrict__ blocks) {
+  const int bits = T.bits;
   const int piece = bits == 2 ? 8 : 16;
-  const int lane_bytes = 4 * bits;
-  const int q_per_lane = lane_bytes / piece;               // pieces per lane per row
-  const int64_t pieces_per_block = 2LL * q_per_lane * 32;  // both halves
+  const int pieces_per_tile = code_bytes(bits) / piece;
+  const int mt_n = unit_tiles(bits);
   const int64_t idx = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
-  const int64_t total = n_tiles * n_chunks * pieces_per_block;
+  const int64_t total = n_units * n_chunks * mt_n * pieces_per_tile;
   if (idx >= total) return;
-  const int64_t blk = idx / pieces_per_block;
-  const int p = (int)(idx % pieces_per_block);
-  const int lane = p % 32, hq = p / 32, q = hq % q_per_lane, h = hq / q_per_lane;
-  const int64_t tile = blk / n_chunks, ch = blk % n_chunks;
+  const int p = (int)(idx % pieces_per_tile);
+  int64_t rest = idx / pieces_per_tile;
+  const int mt = (int)(rest % mt_n);
+  rest /= mt_n;
+  const int64_t ch = rest % n_chunks, unit = rest / n_chunks;
+  const int lane = p % 32;
   const int g = lane >> 2, c = lane & 3;
+  int h, q = 0, plane = 0;
+  if (bits == 8) { plane = p / 64; h = (p / 32) % 2; }
+  else if (bits == 16) { h = p / 128; q = (p / 32) % 4; }
+  else { h = p / 32; }
+  const int64_t tile = unit * mt_n + mt;
   const int64_t row = tile * kTileRows + g + 8 * h;
-  uint8_t* dst = blocks + blk * block_bytes(bits) + (int64_t)p * piece;
-  const int64_t col_byte = ch * (16 * bits) + c * lane_bytes + q * piece;
-  if (row < T.n_rows) {
-    const uint8_t* src = T.codes + row * T.row_bytes + col_byte;
-    for (int i = 0; i < piece; ++i) dst[i] = src[i];
+  uint8_t* dst = blocks + (unit * n_chunks + ch) * chunk_bytes(bits) + mt * tile_block_bytes(bits) +
+                 (int64_t)p * piece;
+  const bool live = row < T.n_rows;
+  const int64_t col0 = ch * 128 + c * 32;  // first column of the lane's block
+  if (bits == 4 || bits == 2) {
+    const uint8_t* src = T.codes + row * T.row_bytes + (ch * 16 * bits) + c * (4 * bits);
+    for (int i = 0; i < piece; ++i) dst[i] = live ? src[i] : 0;
+  } else if (bits == 8) {
+    const uint8_t* src = T.codes + row * T.row_bytes + col0;
+    for (int j = 0; j < 16; ++j) {
+      uint32_t b = 0;
+      if (live) {
+        const uint32_t q0 = src[2 * j], q1 = src[2 * j + 1];
+        b = ((q0 >> (4 * plane)) & 15u) | (((q1 >> (4 * plane)) & 15u) << 4);
+      }
+      dst[j] = (uint8_t)b;
+    }
   } else {
-    for (int i = 0; i < piece; ++i) dst[i] = 0;
+    const __half* src = reinterpret_cast<const __half*>(T.codes + row * T.row_bytes) + col0 + 8 * q;
+    uint16_t* d16 = reinterpret_cast<uint16_t*>(dst);  // 16-byte aligned piece
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const int k = (j >> 1) + 4 * (j & 1);  // column order 0, 4, 1, 5, 2, 6, 3, 7
+      float v = live ? __half2float(src[k]) : 0.0f;
+      if (k & 1) v = fminf(fmaxf(v * 16.0f, -65504.0f), 65504.0f);  // "high" positions: x16 (exact)
+      d16[j] = __half_as_ushort(__float2half_rn(v));
+    }
   }
 }
 
-__global__ void repack_meta_kernel(const csaq_tier T, int64_t n_chunks, int bits, int64_t n_tiles,
+__global__ void repack_meta_kernel(const csaq_tier T, int64_t n_chunks, int64_t n_units,
                                    uint8_t* __restrict__ blocks) {
+  const int bits = T.bits;
+  const int mt_n = unit_tiles(bits);
   const int64_t idx = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
-  if (idx >= n_tiles * n_chunks * kTileRows) return;
+  if (idx >= n_units * n_chunks * mt_n * kTileRows) return;
   const int r = (int)(idx % kTileRows);
-  const int64_t blk = idx / kTileRows;
-  const int64_t tile = blk / n_chunks, ch = blk % n_chunks;
-  const int64_t row = tile * kTileRows + r;
+  int64_t rest = idx / kTileRows;
+  const int mt = (int)(rest % mt_n);
+  rest /= mt_n;
+  const int64_t ch = rest % n_chunks, unit = rest / n_chunks;
+  const int64_t row = (unit * mt_n + mt) * kTileRows + r;
   const int64_t gi = (T.n_groups > 1) ? (ch * 128) / T.group_size : 0;
-  uint8_t* meta = blocks + blk * block_bytes(bits) + 16 * 16 * bits;
+  uint8_t* meta = blocks + (unit * n_chunks + ch) * chunk_bytes(bits) + mt * tile_block_bytes(bits) +
+                  code_bytes(bits);
   float s = 0.0f;
   uint8_t z = 0;
   if (row < T.n_rows) {
@@ -152,15 +182,16 @@ __global__ void repack_meta_kernel(const csaq_tier T, int64_t n_chunks, int bits
 }
 
 // ── activation records ──────────────────────────────────────────────────────
-// Per 32-column lane block, 8 records (b0, b1) of fp16 pairs:
-//   4-bit, word m (cols 8m..8m+7): [2m] = ((x0,x4),(x1/16,x5/16)), [2m+1] = ((x2,x6),(x3/16,x7/16))
-//   8-bit, word m (cols 4m..4m+3): [m]  = ((x0,x2),(x1,x3))
-//   2-bit, word m (cols 16m..16m+15), t = 0..3:
-//          [4m+t] = ((x_{2t}/f,x_{2t+8}/f),(x_{2t+1}/f',x_{2t+9}/f')), (f, f') = (1,4),(16,64),(1,4),(16,64)
-//   16-bit: [s] = ((x_{4s},x_{4s+1}),(x_{4s+2},x_{4s+3}))
-template <int BITS, typename ACT>
-__device__ __forceinline__ void build_records(const ACT* __restrict__ xrow, float inv, uint2 (&rec)[8],
-                                              float& C, float& S) {
+// R4 (4/8/16-bit tiers), per 32-column lane block, word m = cols 8m..8m+7:
+//   [2m] = ((x0,x4),(x1/16,x5/16)), [2m+1] = ((x2,x6),(x3/16,x7/16))
+//   C4 = 1024 (x0+x4+x2+x6) + 64 (x1+x5+x3+x7) summed over the chunk
+// R2 (2-bit tiers), word m = cols 16m..16m+15, t = 0..3:
+//   [4m+t] = ((x_{2t}/f,x_{2t+8}/f),(x_{2t+1}/f',x_{2t+9}/f')), (f,f') = (1,4),(16,64),(1,4),(16,64)
+//   C2 = sum (1024 / f) x
+template <typename ACT>
+__device__ __forceinline__ void build_records(const ACT* __restrict__ xrow, float inv, bool want2,
+                                              uint2 (&r4)[8], uint2 (&r2)[8], float& C4, float& C2,
+                                              float& S) {
   float v[32];
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
@@ -169,22 +200,18 @@ __device__ __forceinline__ void build_records(const ACT* __restrict__ xrow, floa
 #pragma unroll
     for (int j = 0; j < 8; ++j) v[8 * i + j] = to_f32<ACT>(e[j]) * inv;  // exact power-of-two scaling
   }
-  float s = 0.0f, c = 0.0f;
-  if constexpr (BITS == 4) {
+  float c4 = 0.0f, s = 0.0f;
 #pragma unroll
-    for (int m = 0; m < 4; ++m) {
-      const float* x = v + 8 * m;
-      rec[2 * m] = make_uint2(pack_h2(x[0], x[4]), pack_h2(x[1] * 0.0625f, x[5] * 0.0625f));
-      rec[2 * m + 1] = make_uint2(pack_h2(x[2], x[6]), pack_h2(x[3] * 0.0625f, x[7] * 0.0625f));
-      c += 1024.0f * (x[0] + x[4] + x[2] + x[6]) + 64.0f * (x[1] + x[5] + x[3] + x[7]);
-    }
-  } else if constexpr (BITS == 8) {
+  for (int m = 0; m < 4; ++m) {
+    const float* x = v + 8 * m;
+    r4[2 * m] = make_uint2(pack_h2(x[0], x[4]), pack_h2(x[1] * 0.0625f, x[5] * 0.0625f));
+    r4[2 * m + 1] = make_uint2(pack_h2(x[2], x[6]), pack_h2(x[3] * 0.0625f, x[7] * 0.0625f));
+    c4 += 1024.0f * (x[0] + x[4] + x[2] + x[6]) + 64.0f * (x[1] + x[5] + x[3] + x[7]);
+  }
 #pragma unroll
-    for (int m = 0; m < 8; ++m) {
-      const float* x = v + 4 * m;
-      rec[m] = make_uint2(pack_h2(x[0], x[2]), pack_h2(x[1], x[3]));
-    }
-  } else if constexpr (BITS == 2) {
+  for (int i = 0; i < 32; ++i) s += v[i];
+  float c2 = 0.0f;
+  if (want2) {
     const float f[4] = {1.0f, 0.0625f, 1.0f, 0.0625f};
     const float f2[4] = {0.25f, 0.015625f, 0.25f, 0.015625f};
     const float cf[4] = {1024.0f, 64.0f, 1024.0f, 64.0f};
@@ -194,175 +221,351 @@ __device__ __forceinline__ void build_records(const ACT* __restrict__ xrow, floa
 #pragma unroll
       for (int t = 0; t < 4; ++t) {
         const float* x = v + 16 * m;
-        rec[4 * m + t] = make_uint2(pack_h2(x[2 * t] * f[t], x[2 * t + 8] * f[t]),
-                                    pack_h2(x[2 * t + 1] * f2[t], x[2 * t + 9] * f2[t]));
-        c += cf[t] * (x[2 * t] + x[2 * t + 8]) + cf2[t] * (x[2 * t + 1] + x[2 * t + 9]);
+        r2[4 * m + t] = make_uint2(pack_h2(x[2 * t] * f[t], x[2 * t + 8] * f[t]),
+                                   pack_h2(x[2 * t + 1] * f2[t], x[2 * t + 9] * f2[t]));
+        c2 += cf[t] * (x[2 * t] + x[2 * t + 8]) + cf2[t] * (x[2 * t + 1] + x[2 * t + 9]);
       }
-  } else {
-#pragma unroll
-    for (int j = 0; j < 8; ++j)
-      rec[j] = make_uint2(pack_h2(v[4 * j], v[4 * j + 1]), pack_h2(v[4 * j + 2], v[4 * j + 3]));
   }
-#pragma unroll
-  for (int i = 0; i < 32; ++i) s += v[i];
-  if constexpr (BITS == 8) c = 1024.0f * s;
-  C = c;
+  C4 = c4;
+  C2 = c2;
   S = s;
 }
 
-// MMA over one chunk for the MT tiles of an item (rows g and g+8 of each):
-// the tiles' MMAs are interleaved and each tile alternates between two
-// accumulators, so 2*MT independent chains share the tensor pipe.
-template <int BITS, int MT>
-__device__ __forceinline__ void chunk_mma(const uint32_t (&cw)[MT][2][BITS], const uint2 (&rec)[8],
-                                          float (&g)[MT][2][4]) {
-  constexpr uint32_t M = 0x64006400u;  // fp16 1024.0 in both halves
-  if constexpr (BITS == 4) {
+// ── MMA over one chunk ──────────────────────────────────────────────────────
+constexpr uint32_t kMagic = 0x64006400u;  // fp16 1024.0 in both halves
+
+// 4-bit (or two 8-bit nibble planes) for two tiles: g[tile][acc], the two
+// accumulators of a tile alternate k-steps
+__device__ __forceinline__ void mma4(const uint32_t (&cw)[2][2][4], const uint2 (&rec)[8],
+                                     float (&g)[2][2][4]) {
 #pragma unroll
-    for (int m = 0; m < 4; ++m) {
-      uint32_t v[MT][2][4];
+  for (int m = 0; m < 4; ++m) {
+    uint32_t v[2][2][4];
 #pragma unroll
-      for (int mt = 0; mt < MT; ++mt)
+    for (int mt = 0; mt < 2; ++mt)
 #pragma unroll
-        for (int r = 0; r < 2; ++r) {
-          const uint32_t w = cw[mt][r][m], t = w >> 8;
-          v[mt][r][0] = lop_and_or(w, 0x000F000Fu, M);  // 1024 + q   (cols 0, 4)
-          v[mt][r][1] = lop_and_or(w, 0x00F000F0u, M);  // 1024 + 16q (cols 1, 5)
-          v[mt][r][2] = lop_and_or(t, 0x000F000Fu, M);  //             (cols 2, 6)
-          v[mt][r][3] = lop_and_or(t, 0x00F000F0u, M);  //             (cols 3, 7)
-        }
-#pragma unroll
-      for (int mt = 0; mt < MT; ++mt)
-        mma_f16(g[mt][0], v[mt][0][0], v[mt][1][0], v[mt][0][1], v[mt][1][1], rec[2 * m].x, rec[2 * m].y);
-#pragma unroll
-      for (int mt = 0; mt < MT; ++mt)
-        mma_f16(g[mt][1], v[mt][0][2], v[mt][1][2], v[mt][0][3], v[mt][1][3], rec[2 * m + 1].x, rec[2 * m + 1].y);
-    }
-  } else if constexpr (BITS == 8) {
-#pragma unroll
-    for (int m = 0; m < 8; ++m) {
-#pragma unroll
-      for (int mt = 0; mt < MT; ++mt) {
-        const uint32_t a0 = prmt(cw[mt][0][m], 0x64646464u, 0x4240), a1 = prmt(cw[mt][1][m], 0x64646464u, 0x4240);
-        const uint32_t a2 = prmt(cw[mt][0][m], 0x64646464u, 0x4341), a3 = prmt(cw[mt][1][m], 0x64646464u, 0x4341);
-        mma_f16(g[mt][m & 1], a0, a1, a2, a3, rec[m].x, rec[m].y);
+      for (int r = 0; r < 2; ++r) {
+        const uint32_t w = cw[mt][r][m], t = w >> 8;
+        v[mt][r][0] = lop_and_or(w, 0x000F000Fu, kMagic);  // 1024 + q   (cols 0, 4)
+        v[mt][r][1] = lop_and_or(w, 0x00F000F0u, kMagic);  // 1024 + 16q (cols 1, 5)
+        v[mt][r][2] = lop_and_or(t, 0x000F000Fu, kMagic);  //             (cols 2, 6)
+        v[mt][r][3] = lop_and_or(t, 0x00F000F0u, kMagic);  //             (cols 3, 7)
       }
-    }
-  } else if constexpr (BITS == 2) {
 #pragma unroll
-    for (int m = 0; m < 2; ++m) {
-      uint32_t v[MT][2][8];
+    for (int mt = 0; mt < 2; ++mt)
+      mma_f16(g[mt][0], v[mt][0][0], v[mt][1][0], v[mt][0][1], v[mt][1][1], rec[2 * m].x, rec[2 * m].y);
 #pragma unroll
-      for (int mt = 0; mt < MT; ++mt)
-#pragma unroll
-        for (int r = 0; r < 2; ++r) {
-          const uint32_t w = cw[mt][r][m], t = w >> 8;
-          v[mt][r][0] = lop_and_or(w, 0x00030003u, M);
-          v[mt][r][1] = lop_and_or(w, 0x000C000Cu, M);
-          v[mt][r][2] = lop_and_or(w, 0x00300030u, M);
-          v[mt][r][3] = lop_and_or(w, 0x00C000C0u, M);
-          v[mt][r][4] = lop_and_or(t, 0x00030003u, M);
-          v[mt][r][5] = lop_and_or(t, 0x000C000Cu, M);
-          v[mt][r][6] = lop_and_or(t, 0x00300030u, M);
-          v[mt][r][7] = lop_and_or(t, 0x00C000C0u, M);
-        }
-#pragma unroll
-      for (int t = 0; t < 4; ++t)
-#pragma unroll
-        for (int mt = 0; mt < MT; ++mt)
-          mma_f16(g[mt][t & 1], v[mt][0][2 * t], v[mt][1][2 * t], v[mt][0][2 * t + 1], v[mt][1][2 * t + 1],
-                  rec[4 * m + t].x, rec[4 * m + t].y);
-    }
-  } else {
-#pragma unroll
-    for (int s = 0; s < 8; ++s)
-#pragma unroll
-      for (int mt = 0; mt < MT; ++mt)
-        mma_f16(g[mt][s & 1], cw[mt][0][2 * s], cw[mt][1][2 * s], cw[mt][0][2 * s + 1], cw[mt][1][2 * s + 1],
-                rec[s].x, rec[s].y);
+    for (int mt = 0; mt < 2; ++mt)
+      mma_f16(g[mt][1], v[mt][0][2], v[mt][1][2], v[mt][0][3], v[mt][1][3], rec[2 * m + 1].x, rec[2 * m + 1].y);
   }
 }
 
-struct LaunchCfg {
-  int x_bytes;   // activation records: 2 * M * K
-  int cs_bytes;  // (C, S) per (chunk, token)
-  int ring_div;  // 1: full ring; 2: half ring (large activations)
-  int smem_bytes;
+// 2-bit, two tiles
+__device__ __forceinline__ void mma2(const uint32_t (&cw)[2][2][2], const uint2 (&rec)[8],
+                                     float (&g)[2][2][4]) {
+#pragma unroll
+  for (int m = 0; m < 2; ++m) {
+    uint32_t v[2][2][8];
+#pragma unroll
+    for (int mt = 0; mt < 2; ++mt)
+#pragma unroll
+      for (int r = 0; r < 2; ++r) {
+        const uint32_t w = cw[mt][r][m], t = w >> 8;
+        v[mt][r][0] = lop_and_or(w, 0x00030003u, kMagic);
+        v[mt][r][1] = lop_and_or(w, 0x000C000Cu, kMagic);
+        v[mt][r][2] = lop_and_or(w, 0x00300030u, kMagic);
+        v[mt][r][3] = lop_and_or(w, 0x00C000C0u, kMagic);
+        v[mt][r][4] = lop_and_or(t, 0x00030003u, kMagic);
+        v[mt][r][5] = lop_and_or(t, 0x000C000Cu, kMagic);
+        v[mt][r][6] = lop_and_or(t, 0x00300030u, kMagic);
+        v[mt][r][7] = lop_and_or(t, 0x00C000C0u, kMagic);
+      }
+#pragma unroll
+    for (int t = 0; t < 4; ++t)
+#pragma unroll
+      for (int mt = 0; mt < 2; ++mt)
+        mma_f16(g[mt][t & 1], v[mt][0][2 * t], v[mt][1][2 * t], v[mt][0][2 * t + 1], v[mt][1][2 * t + 1],
+                rec[4 * m + t].x, rec[4 * m + t].y);
+  }
+}
+
+// 16-bit (pre-arranged fp16): words [4m], [4m+1] with rec[2m]; [4m+2], [4m+3] with rec[2m+1]
+__device__ __forceinline__ void mma16(const uint32_t (&cw)[2][16], const uint2 (&rec)[8], float (&g)[2][4]) {
+#pragma unroll
+  for (int m = 0; m < 4; ++m) {
+    mma_f16(g[0], cw[0][4 * m], cw[1][4 * m], cw[0][4 * m + 1], cw[1][4 * m + 1], rec[2 * m].x, rec[2 * m].y);
+    mma_f16(g[1], cw[0][4 * m + 2], cw[1][4 * m + 2], cw[0][4 * m + 3], cw[1][4 * m + 3], rec[2 * m + 1].x,
+            rec[2 * m + 1].y);
+  }
+}
+
+// ── kernel parameters ───────────────────────────────────────────────────────
+// Work items are (unit, chunk) pairs, numbered tier by tier and unit-major, so
+// a run of items is a run of consecutive GEMV blocks. Warp w owns items
+// [begin[w], begin[w + 1]); the host cuts the items into runs of equal block
+// bytes. The cut depends only on the tier shapes and the SM count, never on
+// M, so neither does any partial sum.
+constexpr int kMaxCtas = 160;
+constexpr int kMaxWarps = kMaxCtas * 16;
+
+struct TierWork {
+  int bits, mt, n_units;
+  int item0;    // first item of the tier
+  int n_items;  // n_units * n_chunks
+  int ticket0;  // first ticket (one per unit)
 };
 
 struct KParams {
   TierParams tp;
-  int cta_start[CSAQ_MAX_TIERS + 1];  // persistent CTAs per tier
+  TierWork w[CSAQ_MAX_TIERS];
+  int n_items_total;
+  int n_warps;     // W = gridDim.x * kWarps
+  int slot_bytes;  // ring slot: the largest chunk_bytes of the launch
+  int depth;       // ring slots per warp
+  int want2;       // any 2-bit tier (stage R2 records)
+  int x_bytes;     // R4 records: n_chunks * M * kRecStride (R2 the same again when want2)
+  float* contrib;  // [cta][2][32 rows x 16 tokens] sums of units cut by a CTA boundary
+  int* tickets;    // [unit] chunks done so far (zero between launches)
+  int begin[kMaxWarps + 1];
 };
 
-// Tiles per work item: two 16-row tiles share each chunk's activation
-// records and give two independent MMA chains; fp16 tiers keep one (their
-// blocks are already 4 KB).
-template <int BITS> struct Item {
-  static constexpr int kTiles = BITS == 16 ? 1 : 2;
-  static constexpr int kBytes = kTiles * Geo<BITS>::kBlockBytes;
-  static constexpr int kDepth = BITS == 2 ? 8 : BITS == 4 ? 4 : 2;  // ring slots per warp
-};
+__device__ __forceinline__ int tier_of_item(const KParams& P, int item) {
+  int t = 0;
+  while (t + 1 < P.tp.n_tiers && item >= P.w[t + 1].item0) ++t;
+  return t;
+}
 
-__host__ __device__ __forceinline__ int item_tiles(int bits) { return bits == 16 ? 1 : 2; }
+// the warp whose (non-empty) range holds `item`: the largest w with begin[w] <= item
+__device__ __forceinline__ int warp_of_item(const KParams& P, int item) {
+  int lo = 0, hi = P.n_warps - 1;
+  while (lo < hi) {
+    const int mid = (lo + hi + 1) >> 1;
+    if (P.begin[mid] <= item) lo = mid; else hi = mid - 1;
+  }
+  return lo;
+}
 
-template <typename ACT, int NT, int BITS>
-__device__ __forceinline__ void run_tier(const csaq_tier& T, int cta_in_tier, int ctas_in_tier,
-                                         int64_t K, const ACT* __restrict__ x, int M, int64_t ldx,
-                                         uint8_t* smem, const LaunchCfg& cfg) {
-  using G = Geo<BITS>;
-  using I = Item<BITS>;
-  constexpr int MT = I::kTiles;
-  const int depth = I::kDepth / cfg.ring_div;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+template <typename ACT>
+__device__ __forceinline__ void store_out(const csaq_tier& T, int row, int tok, float v, float xe) {
+  v = __fmul_rn(v, xe);
+  const int orow = T.out_rows[row];
+  if (T.bias) v = __fadd_rn(v, to_f32<ACT>(reinterpret_cast<const ACT*>(T.bias)[orow]));
+  if (T.residual)
+    v = __fadd_rn(v, to_f32<ACT>(reinterpret_cast<const ACT*>(T.residual)[(int64_t)tok * T.ldr + orow]));
+  reinterpret_cast<ACT*>(T.y)[(int64_t)tok * T.ldy + orow] = from_f32<ACT>(v);
+}
+
+// ── bulk copies into the per-warp ring (one elected lane; no multicast) ────
+constexpr int kWaitLimit = 1 << 20;  // try_wait rounds before a wait is abandoned
+__device__ unsigned int g_wait_timeouts;
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, int count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mbar_fence_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;\n\tfence.proxy.async.shared::cta;" ::: "memory");
+}
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
+               : "memory");
+}
+__device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+          smem_u32(dst)),
+      "l"(src), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\tselp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// bounded wait for the phase with the given parity; false when abandoned
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
+  for (int i = 0; i < kWaitLimit; ++i)
+    if (mbar_try_wait(bar, parity)) return true;
+  return false;
+}
+
+// One 128-column chunk of one unit: acc[tile][n-tile][fragment] += the chunk's
+// contribution (see the header comment for the algebra).
+template <int NT>
+__device__ __forceinline__ void chunk_math(int bits, const uint8_t* slot, const uint8_t* rbase,
+                                           const float4* xcs_ch, int M, int lane,
+                                           float (&acc)[2][NT][4]) {
   const int g = lane >> 2, c = lane & 3;
-  const int n_chunks = (int)(K / 128);
-  const int n_tiles = (T.n_rows + kTileRows - 1) / kTileRows;
-  const int n_units = (n_tiles + MT - 1) / MT;
-  const int my_units = cta_in_tier < n_units ? (n_units - 1 - cta_in_tier) / ctas_in_tier + 1 : 0;
-  const int cpw = (n_chunks + kWarps - 1) / kWarps;  // items per warp per unit (uniform)
-  const int total = my_units * cpw;
-  constexpr int kRows = MT * kTileRows;
-
-  uint2* xrec = reinterpret_cast<uint2*>(smem);                               // [ch][8][M][4]
-  float2* xcs = reinterpret_cast<float2*>(smem + cfg.x_bytes);                // [ch][M] (C, S)
-  float* xexp = reinterpret_cast<float*>(smem + cfg.x_bytes + cfg.cs_bytes);  // [16] 2^e per token
-  float* red = xexp + 16;                                                     // [warps][kRows][NT*8]
-  uint8_t* ring = reinterpret_cast<uint8_t*>(red + kWarps * 32 * NT * 8) +
-                  (size_t)warp * depth * I::kBytes;
-
-  // issue cursor: unit u covers tiles u*MT .. u*MT+MT-1; the warp's items are
-  // chunks warp, warp+8, ... of each of its units
-  int i_it = 0, i_j = 0, i_slot = 0, i_unit = cta_in_tier;
-  auto issue = [&]() {
-    if (i_it < total) {
-      const int ch = warp + kWarps * i_j;
-      if (ch < n_chunks) {
-        uint8_t* slot = ring + i_slot * I::kBytes;
 #pragma unroll
-        for (int mt = 0; mt < MT; ++mt) {
-          const int tile = i_unit * MT + mt;
-          if (tile < n_tiles) {
-            const uint8_t* src = T.blocks + ((int64_t)tile * n_chunks + ch) * G::kBlockBytes;
-            uint8_t* dst = slot + mt * G::kBlockBytes;
+  for (int nt = 0; nt < NT; ++nt) {
+    const int tok = nt * 8 + g;
+    uint2 rec[8];
+    if (tok < M) {
+      const uint2* rp = reinterpret_cast<const uint2*>(rbase + tok * kRecStride) + c;
 #pragma unroll
-            for (int off = 0; off < G::kBlockBytes; off += 512)
-              if (off + lane * 16 < G::kBlockBytes) cp_async16(dst + off + lane * 16, src + off + lane * 16);
-          }
+      for (int q = 0; q < 8; ++q) rec[q] = rp[4 * q];
+    } else {
+#pragma unroll
+      for (int q = 0; q < 8; ++q) rec[q] = make_uint2(0u, 0u);
+    }
+    const int t0 = nt * 8 + 2 * c;
+    const float4 cs0 = t0 < M ? xcs_ch[t0] : make_float4(0.f, 0.f, 0.f, 0.f);
+    const float4 cs1 = t0 + 1 < M ? xcs_ch[t0 + 1] : make_float4(0.f, 0.f, 0.f, 0.f);
+    if (bits == 4 || bits == 8) {
+      // 4-bit: [tile][h][word]; 8-bit: [nibble plane][h][word] of one tile
+      uint32_t cw[2][2][4];
+      float gg[2][2][4];
+      const int sub = bits == 4 ? tile_block_bytes(4) : 1024;
+#pragma unroll
+      for (int mt = 0; mt < 2; ++mt) {
+        const uint4* cp = reinterpret_cast<const uint4*>(slot + mt * sub);
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          const uint4 v = cp[h * 32 + lane];
+          cw[mt][h][0] = v.x; cw[mt][h][1] = v.y; cw[mt][h][2] = v.z; cw[mt][h][3] = v.w;
         }
+#pragma unroll
+        for (int a = 0; a < 2; ++a) gg[mt][a][0] = gg[mt][a][1] = gg[mt][a][2] = gg[mt][a][3] = 0.0f;
       }
-      ++i_it;
-      i_slot = (i_slot + 1 == depth) ? 0 : i_slot + 1;
-      if (++i_j == cpw) {
-        i_j = 0;
-        i_unit += ctas_in_tier;
+      mma4(cw, rec, gg);
+      if (bits == 4) {
+#pragma unroll
+        for (int mt = 0; mt < 2; ++mt) {
+          const uint8_t* meta = slot + mt * tile_block_bytes(4) + code_bytes(4);
+          const float s0 = reinterpret_cast<const float*>(meta)[g], s1 = reinterpret_cast<const float*>(meta)[g + 8];
+          const float z0 = (float)meta[64 + g], z1 = (float)meta[64 + g + 8];
+          const float d0 = gg[mt][0][0] + gg[mt][1][0], d1 = gg[mt][0][1] + gg[mt][1][1];
+          const float d2 = gg[mt][0][2] + gg[mt][1][2], d3 = gg[mt][0][3] + gg[mt][1][3];
+          acc[mt][nt][0] = fmaf(s0, fmaf(-z0, cs0.y, d0 - cs0.x), acc[mt][nt][0]);
+          acc[mt][nt][1] = fmaf(s0, fmaf(-z0, cs1.y, d1 - cs1.x), acc[mt][nt][1]);
+          acc[mt][nt][2] = fmaf(s1, fmaf(-z1, cs0.y, d2 - cs0.x), acc[mt][nt][2]);
+          acc[mt][nt][3] = fmaf(s1, fmaf(-z1, cs1.y, d3 - cs1.x), acc[mt][nt][3]);
+        }
+      } else {
+        const uint8_t* meta = slot + code_bytes(8);
+        const float s0 = reinterpret_cast<const float*>(meta)[g], s1 = reinterpret_cast<const float*>(meta)[g + 8];
+        const float z0 = (float)meta[64 + g], z1 = (float)meta[64 + g + 8];
+        float d[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float lo = gg[0][0][e] + gg[0][1][e], hi = gg[1][0][e] + gg[1][1][e];
+          const float C = (e & 1) ? cs1.x : cs0.x;
+          d[e] = fmaf(16.0f, hi - C, lo - C);
+        }
+        acc[0][nt][0] = fmaf(s0, fmaf(-z0, cs0.y, d[0]), acc[0][nt][0]);
+        acc[0][nt][1] = fmaf(s0, fmaf(-z0, cs1.y, d[1]), acc[0][nt][1]);
+        acc[0][nt][2] = fmaf(s1, fmaf(-z1, cs0.y, d[2]), acc[0][nt][2]);
+        acc[0][nt][3] = fmaf(s1, fmaf(-z1, cs1.y, d[3]), acc[0][nt][3]);
+      }
+    } else if (bits == 16) {
+      uint32_t cw[2][16];
+      float gg[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+      const uint4* cp = reinterpret_cast<const uint4*>(slot);
+#pragma unroll
+      for (int h = 0; h < 2; ++h)
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const uint4 v = cp[(h * 4 + q) * 32 + lane];
+          cw[h][4 * q] = v.x; cw[h][4 * q + 1] = v.y; cw[h][4 * q + 2] = v.z; cw[h][4 * q + 3] = v.w;
+        }
+      mma16(cw, rec, gg);
+#pragma unroll
+      for (int e = 0; e < 4; ++e) acc[0][nt][e] += gg[0][e] + gg[1][e];
+    } else {  // 2-bit
+      uint32_t cw[2][2][2];
+      float gg[2][2][4];
+#pragma unroll
+      for (int mt = 0; mt < 2; ++mt) {
+        const uint2* cp = reinterpret_cast<const uint2*>(slot + mt * tile_block_bytes(2));
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          const uint2 v = cp[h * 32 + lane];
+          cw[mt][h][0] = v.x; cw[mt][h][1] = v.y;
+        }
+#pragma unroll
+        for (int a = 0; a < 2; ++a) gg[mt][a][0] = gg[mt][a][1] = gg[mt][a][2] = gg[mt][a][3] = 0.0f;
+      }
+      mma2(cw, rec, gg);
+#pragma unroll
+      for (int mt = 0; mt < 2; ++mt) {
+        const uint8_t* meta = slot + mt * tile_block_bytes(2) + code_bytes(2);
+        const float s0 = reinterpret_cast<const float*>(meta)[g], s1 = reinterpret_cast<const float*>(meta)[g + 8];
+        const float z0 = (float)meta[64 + g], z1 = (float)meta[64 + g + 8];
+        const float d0 = gg[mt][0][0] + gg[mt][1][0], d1 = gg[mt][0][1] + gg[mt][1][1];
+        const float d2 = gg[mt][0][2] + gg[mt][1][2], d3 = gg[mt][0][3] + gg[mt][1][3];
+        acc[mt][nt][0] = fmaf(s0, fmaf(-z0, cs0.y, d0 - cs0.z), acc[mt][nt][0]);
+        acc[mt][nt][1] = fmaf(s0, fmaf(-z0, cs1.y, d1 - cs1.z), acc[mt][nt][1]);
+        acc[mt][nt][2] = fmaf(s1, fmaf(-z1, cs0.y, d2 - cs0.z), acc[mt][nt][2]);
+        acc[mt][nt][3] = fmaf(s1, fmaf(-z1, cs1.y, d3 - cs1.z), acc[mt][nt][3]);
       }
     }
-    cp_async_commit();
-  };
+  }
+}
 
-  // prologue: weights first (they do not depend on the activation)
-  for (int it = 0; it < depth; ++it) issue();
+// fragment (tile mt, n-tile nt, element e) -> (row in unit, token)
+__device__ __forceinline__ int frag_row(int mt, int e, int lane) { return mt * kTileRows + (lane >> 2) + ((e >> 1) << 3); }
+__device__ __forceinline__ int frag_tok(int nt, int e, int lane) { return nt * 8 + 2 * (lane & 3) + (e & 1); }
+
+// a unit of the launch, addressed by tier and index within the tier
+struct UnitRef {
+  int t, unit, start, end;  // items [start, end)
+};
+
+template <typename ACT, int NT>
+__global__ void __launch_bounds__(kThreads, 1) qgemv_mma_kernel(const __grid_constant__ KParams P,
+                                                                int64_t K, const ACT* __restrict__ x,
+                                                                int M, int64_t ldx) {
+  extern __shared__ __align__(16) uint8_t smem[];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int n_chunks = (int)(K / 128);
+
+  uint8_t* rec4 = smem;                                          // [ch][tok] x kRecStride
+  uint8_t* rec2 = smem + P.x_bytes;                              // same layout, 2-bit records
+  float4* xcs = reinterpret_cast<float4*>(smem + (P.want2 ? 2 : 1) * P.x_bytes);  // [ch][tok] (C4, S, C2, -)
+  float* xexp = reinterpret_cast<float*>(xcs + n_chunks * M);    // [16] 2^e per token
+  uint64_t* bars = reinterpret_cast<uint64_t*>(xexp + 16) + warp * 8;  // [warp][8] ring barriers
+  uint8_t* ring_all = reinterpret_cast<uint8_t*>(xexp + 16) + kWarps * 8 * sizeof(uint64_t);
+  uint8_t* ring = ring_all + (size_t)warp * P.depth * P.slot_bytes;
+
+  const int wg = blockIdx.x * kWarps + warp;
+  const int it_begin = P.begin[wg];
+  const int it_end = P.begin[wg + 1];
+  const int cta_begin = P.begin[blockIdx.x * kWarps];
+  const int cta_end = P.begin[(blockIdx.x + 1) * kWarps];
+
+  if (lane == 0) {
+    for (int s = 0; s < P.depth; ++s) mbar_init(&bars[s], 1);
+    mbar_fence_init();
+  }
+  __syncwarp();
+
+  // issue cursor: walks the warp's items (consecutive blocks of each tier)
+  int i_left = it_end - it_begin, i_local = 0;
+  int i_t = 0, i_slot = 0;
+  if (i_left > 0) {
+    i_t = tier_of_item(P, it_begin);
+    i_local = it_begin - P.w[i_t].item0;
+  }
+  auto issue = [&]() {
+    if (i_left > 0) {
+      if (lane == 0) {
+        const int cb = chunk_bytes(P.w[i_t].bits);
+        mbar_expect_tx(&bars[i_slot], (uint32_t)cb);
+        bulk_load(ring + i_slot * P.slot_bytes, P.tp.t[i_t].blocks + (int64_t)i_local * cb, (uint32_t)cb,
+                  &bars[i_slot]);
+      }
+      --i_left;
+      if (++i_local == P.w[i_t].n_items) {
+        i_local = 0;
+        do { ++i_t; } while (i_left > 0 && P.w[i_t].n_items == 0);
+      }
+      i_slot = (i_slot + 1 == P.depth) ? 0 : i_slot + 1;
+    }
+  };
+  for (int d = 0; d < P.depth; ++d) issue();  // weights first: they do not depend on x
 
   // token scales: e_t with max|x_t| * 2^-e_t in [2^14, 2^15)
   uint32_t* smax = reinterpret_cast<uint32_t*>(xexp);
@@ -382,179 +585,207 @@ __device__ __forceinline__ void run_tier(const csaq_tier& T, int cta_in_tier, in
   if (threadIdx.x < 16) {
     const uint32_t b = smax[threadIdx.x];
     const int E = (int)((b >> 23) & 0xFF) - 127;
-    xexp[threadIdx.x] = ldexpf(1.0f, b == 0u ? 0 : E - 14);  // 2^e (the output factor)
+    xexp[threadIdx.x] = ldexpf(1.0f, b == 0u ? 0 : E - 14);  // 2^e: the output factor
   }
   __syncthreads();
 
-  // stage activation records; whole warps iterate together (4-lane shuffles)
+  // activation records (whole warps iterate: 4-lane shuffles)
   const int n_st = M * n_chunks * 4;
   for (int base = 0; base < n_st; base += blockDim.x) {
     const int u = base + threadIdx.x;
     const bool live = u < n_st;
-    const int cc = u & 3;
-    const int rest = u >> 2;
+    const int cc = u & 3, rest = u >> 2;
     const int tok = live ? rest % M : 0, ch = live ? rest / M : 0;
-    uint2 rec[8];
-    float Cv = 0.0f, Sv = 0.0f;
-    if (live) {
-      const float inv = 1.0f / xexp[tok];  // exact: a power of two
-      build_records<BITS, ACT>(x + (int64_t)tok * ldx + ch * 128 + cc * 32, inv, rec, Cv, Sv);
-    }
-    Cv += __shfl_xor_sync(0xffffffffu, Cv, 1);
-    Cv += __shfl_xor_sync(0xffffffffu, Cv, 2);
-    Sv += __shfl_xor_sync(0xffffffffu, Sv, 1);
-    Sv += __shfl_xor_sync(0xffffffffu, Sv, 2);
-    if (live) {
+    uint2 r4[8], r2[8];
+    float C4 = 0.0f, C2 = 0.0f, S = 0.0f;
+    if (live) build_records<ACT>(x + (int64_t)tok * ldx + ch * 128 + cc * 32, 1.0f / xexp[tok],
+                                 P.want2 != 0, r4, r2, C4, C2, S);
 #pragma unroll
-      for (int j = 0; j < 8; ++j) xrec[((ch * 8 + j) * M + tok) * 4 + cc] = rec[j];
-      if (cc == 0) xcs[ch * M + tok] = make_float2(Cv, Sv);
+    for (int o = 1; o < 4; o <<= 1) {
+      C4 += __shfl_xor_sync(0xffffffffu, C4, o);
+      C2 += __shfl_xor_sync(0xffffffffu, C2, o);
+      S += __shfl_xor_sync(0xffffffffu, S, o);
+    }
+    if (live) {
+      uint2* d4 = reinterpret_cast<uint2*>(rec4 + ((int64_t)ch * M + tok) * kRecStride) + cc;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) d4[4 * j] = r4[j];
+      if (P.want2) {
+        uint2* d2 = reinterpret_cast<uint2*>(rec2 + ((int64_t)ch * M + tok) * kRecStride) + cc;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) d2[4 * j] = r2[j];
+      }
+      if (cc == 0) xcs[ch * M + tok] = make_float4(C4, S, C2, 0.0f);
     }
   }
   __syncthreads();
 
-  float acc[MT][NT][4];
+  // ── main loop over the warp's units ──────────────────────────────────────
+  float acc[2][NT][4], fst[2][NT][4];
+  UnitRef split[2] = {{-1, 0, 0, 0}, {-1, 0, 0, 0}};  // [0]: first unit, [1]: last unit (when cut)
+  uint32_t phase = 0;                                  // parity bit per ring slot
+  uint32_t late = 0, late_parity = 0;                 // slots whose wait was abandoned
+  int c_slot = 0;
+  int item = it_begin, local = 0, t = 0;
+  if (item < it_end) {
+    t = tier_of_item(P, item);
+    local = item - P.w[t].item0;
+  }
+  while (item < it_end) {
+    const TierWork& tw = P.w[t];
+    const csaq_tier& T = P.tp.t[t];
+    const int unit = local / n_chunks;
+    const int ch_first = local - unit * n_chunks;
+    const int room = it_end - item;
+    const int ch_last = room < n_chunks - ch_first ? ch_first + room : n_chunks;
 #pragma unroll
-  for (int mt = 0; mt < MT; ++mt)
+    for (int a = 0; a < 2; ++a)
 #pragma unroll
-    for (int nt = 0; nt < NT; ++nt) acc[mt][nt][0] = acc[mt][nt][1] = acc[mt][nt][2] = acc[mt][nt][3] = 0.0f;
+      for (int nt = 0; nt < NT; ++nt) acc[a][nt][0] = acc[a][nt][1] = acc[a][nt][2] = acc[a][nt][3] = 0.0f;
 
-  int c_j = 0, c_slot = 0, c_unit = cta_in_tier;
-  for (int it = 0; it < total; ++it) {
-    const int ch = warp + kWarps * c_j;
-    if constexpr (I::kDepth == 8) {
-      if (cfg.ring_div == 1) cp_async_wait<7>(); else cp_async_wait<3>();
-    } else if constexpr (I::kDepth == 4) {
-      if (cfg.ring_div == 1) cp_async_wait<3>(); else cp_async_wait<1>();
-    } else {
-      if (cfg.ring_div == 1) cp_async_wait<1>(); else cp_async_wait<0>();
+    for (int ch = ch_first; ch < ch_last; ++ch) {
+      if (!mbar_wait(&bars[c_slot], (phase >> c_slot) & 1u)) {
+        late |= 1u << c_slot;
+        late_parity = (late_parity & ~(1u << c_slot)) | (phase & (1u << c_slot));
+      }
+      phase ^= 1u << c_slot;
+      chunk_math<NT>(tw.bits, ring + c_slot * P.slot_bytes,
+                     (tw.bits == 2 ? rec2 : rec4) + (int64_t)ch * M * kRecStride, xcs + ch * M, M, lane, acc);
+      __syncwarp();
+      issue();
+      c_slot = (c_slot + 1 == P.depth) ? 0 : c_slot + 1;
     }
-    __syncwarp();
-    if (ch < n_chunks) {
-      const uint8_t* slot = ring + c_slot * I::kBytes;
-      // activation records of this chunk, shared by the item's tiles
-      const uint2* xr = xrec + (ch * 8 * M) * 4 + c;
-      uint2 rec[NT][8];
-#pragma unroll
-      for (int nt = 0; nt < NT; ++nt) {
-        const int tok = nt * 8 + g;
-#pragma unroll
-        for (int q = 0; q < 8; ++q) rec[nt][q] = tok < M ? xr[(q * M + tok) * 4] : make_uint2(0u, 0u);
-      }
-      float2 cs[NT][2];
-#pragma unroll
-      for (int nt = 0; nt < NT; ++nt) {
-        const int t0 = nt * 8 + 2 * c;
-        cs[nt][0] = (BITS != 16 && t0 < M) ? xcs[ch * M + t0] : make_float2(0.0f, 0.0f);
-        cs[nt][1] = (BITS != 16 && t0 + 1 < M) ? xcs[ch * M + t0 + 1] : make_float2(0.0f, 0.0f);
-      }
-      // codes and metadata of the item's tiles (a missing second tile reads a
-      // stale slot; its rows lie past n_rows and are never stored)
-      uint32_t cw[MT][2][BITS];
-      float sm[MT][2], zm[MT][2];
-#pragma unroll
-      for (int mt = 0; mt < MT; ++mt) {
-        const uint8_t* blk = slot + mt * G::kBlockBytes;
-#pragma unroll
-        for (int h = 0; h < 2; ++h) {
-          if constexpr (BITS == 2) {
-            const uint2 v = reinterpret_cast<const uint2*>(blk)[h * 32 + lane];
-            cw[mt][h][0] = v.x; cw[mt][h][1] = v.y;
-          } else {
-#pragma unroll
-            for (int q = 0; q < BITS / 4; ++q) {
-              const uint4 v = reinterpret_cast<const uint4*>(blk)[(h * (BITS / 4) + q) * 32 + lane];
-              cw[mt][h][4 * q] = v.x; cw[mt][h][4 * q + 1] = v.y; cw[mt][h][4 * q + 2] = v.z; cw[mt][h][4 * q + 3] = v.w;
-            }
-          }
-        }
-        sm[mt][0] = sm[mt][1] = 1.0f;
-        zm[mt][0] = zm[mt][1] = 0.0f;
-        if constexpr (BITS != 16) {
-          const float* sc = reinterpret_cast<const float*>(blk + G::kCodeBytes);
-          const uint8_t* zp = blk + G::kCodeBytes + 64;
-          sm[mt][0] = sc[g]; sm[mt][1] = sc[g + 8];
-          zm[mt][0] = (float)zp[g]; zm[mt][1] = (float)zp[g + 8];
-        }
-      }
-#pragma unroll
-      for (int nt = 0; nt < NT; ++nt) {
-        float gs[MT][2][4];
-#pragma unroll
-        for (int mt = 0; mt < MT; ++mt)
-#pragma unroll
-          for (int a = 0; a < 2; ++a) gs[mt][a][0] = gs[mt][a][1] = gs[mt][a][2] = gs[mt][a][3] = 0.0f;
-        chunk_mma<BITS, MT>(cw, rec[nt], gs);
-#pragma unroll
-        for (int mt = 0; mt < MT; ++mt) {
-          const float g0 = gs[mt][0][0] + gs[mt][1][0], g1 = gs[mt][0][1] + gs[mt][1][1];
-          const float g2 = gs[mt][0][2] + gs[mt][1][2], g3 = gs[mt][0][3] + gs[mt][1][3];
-          if constexpr (BITS == 16) {
-            acc[mt][nt][0] += g0; acc[mt][nt][1] += g1; acc[mt][nt][2] += g2; acc[mt][nt][3] += g3;
-          } else {
-            acc[mt][nt][0] = fmaf(sm[mt][0], fmaf(-zm[mt][0], cs[nt][0].y, g0 - cs[nt][0].x), acc[mt][nt][0]);
-            acc[mt][nt][1] = fmaf(sm[mt][0], fmaf(-zm[mt][0], cs[nt][1].y, g1 - cs[nt][1].x), acc[mt][nt][1]);
-            acc[mt][nt][2] = fmaf(sm[mt][1], fmaf(-zm[mt][1], cs[nt][0].y, g2 - cs[nt][0].x), acc[mt][nt][2]);
-            acc[mt][nt][3] = fmaf(sm[mt][1], fmaf(-zm[mt][1], cs[nt][1].y, g3 - cs[nt][1].x), acc[mt][nt][3]);
-          }
-        }
-      }
-    }
-    __syncwarp();
-    issue();
-    c_slot = (c_slot + 1 == depth) ? 0 : c_slot + 1;
 
-    if (c_j == cpw - 1) {  // end of a unit: reduce the warps' K slices
-      float* rw = red + warp * kRows * NT * 8;
+    const int u_start = tw.item0 + unit * n_chunks;
+    if (ch_first == 0 && ch_last == n_chunks) {
+      // the whole unit is in this warp: write y from the fragments
 #pragma unroll
-      for (int mt = 0; mt < MT; ++mt)
+      for (int mt = 0; mt < 2; ++mt)
 #pragma unroll
-        for (int nt = 0; nt < NT; ++nt) {
-          const int r0 = mt * kTileRows + g;
-          rw[r0 * NT * 8 + nt * 8 + 2 * c] = acc[mt][nt][0];
-          rw[r0 * NT * 8 + nt * 8 + 2 * c + 1] = acc[mt][nt][1];
-          rw[(r0 + 8) * NT * 8 + nt * 8 + 2 * c] = acc[mt][nt][2];
-          rw[(r0 + 8) * NT * 8 + nt * 8 + 2 * c + 1] = acc[mt][nt][3];
-          acc[mt][nt][0] = acc[mt][nt][1] = acc[mt][nt][2] = acc[mt][nt][3] = 0.0f;
-        }
-      __syncthreads();
-      for (int i = threadIdx.x; i < kRows * NT * 8; i += blockDim.x) {
-        const int r = i / (NT * 8), tok = i % (NT * 8);
-        const int row = c_unit * kRows + r;
-        if (row >= T.n_rows || tok >= M) continue;
-        float v = 0.0f;
+        for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
-        for (int w = 0; w < kWarps; ++w) v += red[w * kRows * NT * 8 + i];
-        v *= xexp[tok];
-        const int orow = T.out_rows[row];
-        if (T.bias) v += to_f32<ACT>(reinterpret_cast<const ACT*>(T.bias)[orow]);
-        if (T.residual) v += to_f32<ACT>(reinterpret_cast<const ACT*>(T.residual)[(int64_t)tok * T.ldr + orow]);
-        reinterpret_cast<ACT*>(T.y)[(int64_t)tok * T.ldy + orow] = from_f32<ACT>(v);
-      }
-      __syncthreads();
-      c_j = 0;
-      c_unit += ctas_in_tier;
+          for (int e = 0; e < 4; ++e) {
+            const int row = unit * tw.mt * kTileRows + frag_row(mt, e, lane), tok = frag_tok(nt, e, lane);
+            if (mt < tw.mt && tok < M && row < T.n_rows) store_out<ACT>(T, row, tok, acc[mt][nt][e], xexp[tok]);
+          }
+    } else if (item == it_begin) {
+      split[0] = {t, unit, u_start, u_start + n_chunks};
+#pragma unroll
+      for (int a = 0; a < 2; ++a)
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+          for (int e = 0; e < 4; ++e) fst[a][nt][e] = acc[a][nt][e];
     } else {
-      ++c_j;
+      split[1] = {t, unit, u_start, u_start + n_chunks};  // the last unit: stays in acc
+    }
+
+    item += ch_last - ch_first;
+    local += ch_last - ch_first;
+    if (local == tw.n_items) {
+      local = 0;
+      do { ++t; } while (item < it_end && P.w[t].n_items == 0);
     }
   }
-  cp_async_wait<0>();
-}
+  if (late) {
+    if (lane == 0) atomicAdd(&g_wait_timeouts, 1u);
+    // let the abandoned copies land (again bounded) before shared memory is reused
+    for (int s = 0; s < P.depth; ++s)
+      if (late & (1u << s)) mbar_wait(&bars[s], (late_parity >> s) & 1u);
+  }
 
-template <typename ACT, int NT>
-__global__ void __launch_bounds__(kThreads) qgemv_mma_kernel(const __grid_constant__ KParams P,
-                                                             int64_t K, const ACT* __restrict__ x,
-                                                             int M, int64_t ldx, LaunchCfg cfg) {
-  extern __shared__ __align__(16) uint8_t smem[];
-  int ti = 0;
-  while (ti + 1 < P.tp.n_tiers && (int)blockIdx.x >= P.cta_start[ti + 1]) ++ti;
-  const csaq_tier& T = P.tp.t[ti];
-  const int cta = blockIdx.x - P.cta_start[ti];
-  const int nct = P.cta_start[ti + 1] - P.cta_start[ti];
-  switch (T.bits) {
-    case 4: run_tier<ACT, NT, 4>(T, cta, nct, K, x, M, ldx, smem, cfg); break;
-    case 8: run_tier<ACT, NT, 8>(T, cta, nct, K, x, M, ldx, smem, cfg); break;
-    case 2: run_tier<ACT, NT, 2>(T, cta, nct, K, x, M, ldx, smem, cfg); break;
-    default: run_tier<ACT, NT, 16>(T, cta, nct, K, x, M, ldx, smem, cfg); break;
+  // ── cut units: partials of the CTA's warps meet in shared memory ──────────
+  __syncthreads();  // every ring is drained
+  float* part = reinterpret_cast<float*>(ring_all);  // [warp][2][32 rows][M]
+#pragma unroll
+  for (int s = 0; s < 2; ++s) {
+    if (split[s].t < 0) continue;
+    float* dst = part + (warp * 2 + s) * 32 * M;
+#pragma unroll
+    for (int mt = 0; mt < 2; ++mt)
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int tok = frag_tok(nt, e, lane);
+          if (mt < P.w[split[s].t].mt && tok < M)
+            dst[frag_row(mt, e, lane) * M + tok] = s == 0 ? fst[mt][nt][e] : acc[mt][nt][e];
+        }
+  }
+  __syncthreads();
+
+#pragma unroll 1
+  for (int s = 0; s < 2; ++s) {
+    const UnitRef u = split[s];
+    if (u.t < 0) continue;
+    // the highest warp of this CTA holding part of the unit reduces it
+    if (P.begin[wg + 1] < min(u.end, cta_end)) continue;
+    const TierWork& tw = P.w[u.t];
+    const csaq_tier& T = P.tp.t[u.t];
+    const int rows = tw.mt * kTileRows;
+    const int n_val = rows * M, nv = (n_val + 31) >> 5;  // values per lane: e = lane + 32 j
+    float v[16];
+#pragma unroll
+    for (int j = 0; j < 16; ++j) v[j] = 0.0f;
+    const int w0 = warp_of_item(P, max(u.start, cta_begin));
+    for (int w = w0; w <= wg; ++w) {
+      const int b = P.begin[w];
+      if (b == P.begin[w + 1]) continue;  // empty range
+      const float* src = part + ((w - blockIdx.x * kWarps) * 2 + (b >= u.start ? 0 : 1)) * 32 * M;
+#pragma unroll
+      for (int j = 0; j < 16; ++j) {
+        if (j >= nv) break;
+        const int e = lane + 32 * j;
+        if (e < n_val) v[j] += src[e];
+      }
+    }
+    if (u.start >= cta_begin && u.end <= cta_end) {
+#pragma unroll
+      for (int j = 0; j < 16; ++j) {
+        if (j >= nv) break;
+        const int e = lane + 32 * j, r = e / M, tok = e - r * M, row = u.unit * rows + r;
+        if (e < n_val && row < T.n_rows) store_out<ACT>(T, row, tok, v[j], xexp[tok]);
+      }
+      continue;
+    }
+    // the unit crosses a CTA boundary: publish this CTA's sum, take a ticket;
+    // the CTA completing the unit adds the CTA sums in CTA order
+    float* gdst = P.contrib + ((int64_t)blockIdx.x * 2 + (cta_begin >= u.start ? 0 : 1)) * (32 * 16);
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      if (j >= nv) break;
+      const int e = lane + 32 * j;
+      if (e < n_val) __stcg(gdst + e, v[j]);
+    }
+    __threadfence();
+    __syncwarp();
+    const int done = min(u.end, cta_end) - max(u.start, cta_begin);
+    int old = 0;
+    if (lane == 0) old = atomicAdd(P.tickets + tw.ticket0 + u.unit, done);
+    old = __shfl_sync(0xffffffffu, old, 0);
+    if (old + done != n_chunks) continue;
+    __threadfence();
+#pragma unroll
+    for (int j = 0; j < 16; ++j) v[j] = 0.0f;
+    for (int cta = warp_of_item(P, u.start) / kWarps; cta < (int)gridDim.x; ++cta) {
+      const int b = P.begin[cta * kWarps];
+      if (b >= u.end) break;
+      if (b == P.begin[(cta + 1) * kWarps]) continue;  // empty CTA
+      const float* src = P.contrib + ((int64_t)cta * 2 + (b >= u.start ? 0 : 1)) * (32 * 16);
+#pragma unroll
+      for (int j = 0; j < 16; ++j) {
+        if (j >= nv) break;
+        const int e = lane + 32 * j;
+        if (e < n_val) v[j] += __ldcg(src + e);
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      if (j >= nv) break;
+      const int e = lane + 32 * j, r = e / M, tok = e - r * M, row = u.unit * rows + r;
+      if (e < n_val && row < T.n_rows) store_out<ACT>(T, row, tok, v[j], xexp[tok]);
+    }
+    if (lane == 0) P.tickets[tw.ticket0 + u.unit] = 0;  // ready for the next launch
   }
 }
 
@@ -665,104 +896,178 @@ int num_sms() {
 }
 
 constexpr int kSmemBudget = 227 * 1024;
+constexpr int kRingBudget = 12 * 1024;  // bytes of weights in flight per warp (target)
+constexpr int kContribFloats = 2 * 32 * 16;  // per CTA: two units x 32 rows x 16 tokens
 
-int ring_bytes(int div) {
-  int m = 0;
-  const int r[4] = {Item<2>::kDepth * Item<2>::kBytes, Item<4>::kDepth * Item<4>::kBytes,
-                    Item<8>::kDepth * Item<8>::kBytes, Item<16>::kDepth * Item<16>::kBytes};
-  for (int i = 0; i < 4; ++i) m = r[i] > m ? r[i] : m;
-  return kWarps * m / div;
+int grid_ctas_max() { return num_sms() < kMaxCtas ? num_sms() : kMaxCtas; }
+
+// Workspace: per-CTA sums of units cut by a CTA boundary (a fixed region for a
+// given device, so launches of different shapes can share one workspace), then
+// one ticket per unit of every tier, in tier order. Returns -1 when the launch has
+// more work items than the kernel indexes.
+int64_t workspace_layout(const TierParams& TP, int64_t K, TierWork* w, int64_t* tickets_off) {
+  const int64_t n_chunks = K / 128;
+  const int64_t contrib = (int64_t)grid_ctas_max() * kContribFloats * 4;
+  int64_t tk = 0, items = 0;
+  for (int i = 0; i < TP.n_tiers; ++i) {
+    const csaq_tier& t = TP.t[i];
+    const int mt = unit_tiles(t.bits);
+    const int64_t tiles = ((int64_t)t.n_rows + kTileRows - 1) / kTileRows;
+    const int64_t units = (tiles + mt - 1) / mt;
+    if (w) {
+      w[i].bits = t.bits;
+      w[i].mt = mt;
+      w[i].n_units = (int)units;
+      w[i].item0 = (int)items;
+      w[i].n_items = (int)(units * n_chunks);
+      w[i].ticket0 = (int)tk;
+    }
+    tk += units;
+    items += units * n_chunks;
+  }
+  if (items >= (int64_t)1 << 30) return -1;
+  if (tickets_off) *tickets_off = contrib;
+  return contrib + tk * 4;
 }
 
-// Shared memory: activation records (2*M*K), (C, S) per (chunk, token), token
-// scales, the reduction buffer and the per-warp cp.async rings.
-bool plan(int64_t K, int M, int NT, LaunchCfg& cfg) {
-  cfg.x_bytes = (int)(2 * M * K);
-  cfg.cs_bytes = (int)(((K / 128) * M * 8 + 15) / 16 * 16);
-  const int fixed = cfg.x_bytes + cfg.cs_bytes + 64 + kWarps * 32 * NT * 8 * 4;
-  for (int div = 1; div <= 2; div *= 2) {
-    cfg.ring_div = div;
-    cfg.smem_bytes = fixed + ring_bytes(div);
-    if (cfg.smem_bytes <= kSmemBudget) return true;
+// Cut the items into W runs of equal block bytes: warp w starts at the first
+// item whose start cost is >= floor(C w / W). Cached per shape.
+struct PartitionCache {
+  struct Entry {
+    std::vector<int> key;
+    std::vector<int> begin;
+  };
+  std::mutex mu;
+  std::vector<Entry> entries;
+  size_t next = 0;
+};
+
+bool partition(const TierParams& TP, const TierWork* w, int64_t K, int n_warps, int* begin) {
+  static PartitionCache cache;
+  std::vector<int> key;
+  key.reserve(4 + 2 * TP.n_tiers);
+  key.push_back((int)(K / 128));
+  key.push_back(n_warps);
+  key.push_back(TP.n_tiers);
+  for (int i = 0; i < TP.n_tiers; ++i) {
+    key.push_back(TP.t[i].bits);
+    key.push_back(TP.t[i].n_rows);
   }
-  return false;
+  std::lock_guard<std::mutex> lock(cache.mu);
+  for (const auto& e : cache.entries)
+    if (e.key == key) {
+      std::copy(e.begin.begin(), e.begin.end(), begin);
+      return true;
+    }
+  int64_t total = 0;
+  for (int i = 0; i < TP.n_tiers; ++i) total += (int64_t)(chunk_bytes(w[i].bits) / 16) * w[i].n_items;
+  std::vector<int> b(n_warps + 1);
+  int t = 0;
+  int64_t cost0 = 0;  // cost before tier t
+  for (int k = 0; k <= n_warps; ++k) {
+    const int64_t target = total * k / n_warps;
+    while (t < TP.n_tiers && cost0 + (int64_t)(chunk_bytes(w[t].bits) / 16) * w[t].n_items <= target) {
+      cost0 += (int64_t)(chunk_bytes(w[t].bits) / 16) * w[t].n_items;
+      ++t;
+    }
+    if (t == TP.n_tiers || k == n_warps) {
+      b[k] = w[TP.n_tiers - 1].item0 + w[TP.n_tiers - 1].n_items;
+      continue;
+    }
+    const int64_t ic = chunk_bytes(w[t].bits) / 16;
+    const int64_t d = target - cost0;
+    int64_t i = d <= 0 ? 0 : (d + ic - 1) / ic;
+    if (i > w[t].n_items) i = w[t].n_items;
+    b[k] = w[t].item0 + (int)i;
+  }
+  std::copy(b.begin(), b.end(), begin);
+  if (cache.entries.size() < 64) {
+    cache.entries.push_back({key, b});
+  } else {
+    cache.entries[cache.next] = {key, b};
+    cache.next = (cache.next + 1) % cache.entries.size();
+  }
+  return true;
+}
+
+struct Plan {
+  int x_bytes, smem_bytes, depth, slot_bytes, want2;
+};
+
+bool make_plan(const TierParams& TP, int64_t K, int M, Plan& p) {
+  const int n_chunks = (int)(K / 128);
+  p.slot_bytes = 0;
+  p.want2 = 0;
+  for (int i = 0; i < TP.n_tiers; ++i) {
+    if (TP.t[i].n_rows == 0) continue;
+    const int cb = chunk_bytes(TP.t[i].bits);
+    p.slot_bytes = cb > p.slot_bytes ? cb : p.slot_bytes;
+    if (TP.t[i].bits == 2) p.want2 = 1;
+  }
+  if (p.slot_bytes == 0) p.slot_bytes = 16;
+  p.x_bytes = n_chunks * M * kRecStride;
+  // records, (C, S) per chunk and token, 2^e per token, ring barriers
+  const int fixed = (p.want2 ? 2 : 1) * p.x_bytes + n_chunks * M * 16 + 64 + kWarps * 8 * 8;
+  const int part_bytes = kWarps * 2 * 32 * M * 4;  // reuses the rings after the main loop
+  int depth = kRingBudget / p.slot_bytes;
+  depth = depth < 2 ? 2 : (depth > 8 ? 8 : depth);
+  auto ring_bytes = [&](int d) { return kWarps * d * p.slot_bytes > part_bytes ? kWarps * d * p.slot_bytes : part_bytes; };
+  while (depth > 2 && fixed + ring_bytes(depth) > kSmemBudget) --depth;
+  p.depth = depth;
+  p.smem_bytes = fixed + ring_bytes(depth);
+  return p.smem_bytes <= kSmemBudget;
 }
 
 template <typename ACT, int NT>
-int ctas_per_sm(int smem_bytes) {
-  static int cached_smem[8] = {-1, -1, -1, -1, -1, -1, -1, -1};
-  static int cached_val[8];
-  static int next = 0;
-  static bool attr_set = false;
-  for (int i = 0; i < 8; ++i)
-    if (cached_smem[i] == smem_bytes) return cached_val[i];
-  if (!attr_set) {
+int set_smem_attr() {
+  static bool done = false;
+  if (!done) {
     if (cudaFuncSetAttribute(qgemv_mma_kernel<ACT, NT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              kSmemBudget) != cudaSuccess)
-      return -1;
-    attr_set = true;
+      return launch_status();
+    done = true;
   }
-  int per_sm = 0;
-  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, qgemv_mma_kernel<ACT, NT>, kThreads,
-                                                    smem_bytes) != cudaSuccess)
-    return -1;
-  per_sm = per_sm < 1 ? 1 : per_sm;
-  cached_smem[next] = smem_bytes;
-  cached_val[next] = per_sm;
-  next = (next + 1) % 8;
-  return per_sm;
+  return CSAQ_OK;
 }
 
 template <typename ACT, int NT>
 int launch_mma_block(const TierParams& TP, int64_t K, const ACT* x, int M, int64_t ldx,
-                     cudaStream_t st) {
-  LaunchCfg cfg;
-  if (!plan(K, M, NT, cfg)) return CSAQ_ERR_UNSUPPORTED;
-  const int per_sm = ctas_per_sm<ACT, NT>(cfg.smem_bytes);
-  if (per_sm < 0) return launch_status();
-  const int max_ctas = num_sms() * per_sm;
-  KParams P;
+                     void* workspace, cudaStream_t st) {
+  Plan pl;
+  if (!make_plan(TP, K, M, pl)) return CSAQ_ERR_UNSUPPORTED;
+  int rc = set_smem_attr<ACT, NT>();
+  if (rc) return rc;
+  static thread_local KParams P;  // about 12 KB: kept off the stack
   P.tp = TP;
-  // persistent CTAs per tier in proportion to the tier's bytes, at most one
-  // per work unit (item_tiles tiles)
-  double total_bytes = 0.0;
-  int total_units = 0;
-  for (int i = 0; i < TP.n_tiers; ++i) {
-    const csaq_tier& t = TP.t[i];
-    total_bytes += (double)t.n_rows * (double)block_bytes(t.bits);
-    const int tiles = (t.n_rows + kTileRows - 1) / kTileRows;
-    total_units += (tiles + item_tiles(t.bits) - 1) / item_tiles(t.bits);
-  }
-  if (total_units == 0) return CSAQ_OK;
-  const int budget = total_units < max_ctas ? total_units : max_ctas;
-  int ctas = 0;
-  for (int i = 0; i < TP.n_tiers; ++i) {
-    const csaq_tier& t = TP.t[i];
-    const int tiles = (t.n_rows + kTileRows - 1) / kTileRows;
-    const int units = (tiles + item_tiles(t.bits) - 1) / item_tiles(t.bits);
-    int n = 0;
-    if (units > 0) {
-      n = (int)((double)budget * ((double)t.n_rows * (double)block_bytes(t.bits)) / total_bytes + 0.5);
-      n = n < 1 ? 1 : (n > units ? units : n);
-    }
-    P.cta_start[i] = ctas;
-    ctas += n;
-  }
-  P.cta_start[TP.n_tiers] = ctas;
-  qgemv_mma_kernel<ACT, NT><<<ctas, kThreads, cfg.smem_bytes, st>>>(P, K, x, M, ldx, cfg);
+  int64_t tick_off = 0;
+  if (workspace_layout(TP, K, P.w, &tick_off) < 0) return CSAQ_ERR_UNSUPPORTED;
+  P.contrib = reinterpret_cast<float*>(workspace);
+  P.tickets = reinterpret_cast<int*>(reinterpret_cast<uint8_t*>(workspace) + tick_off);
+  const int items = P.w[TP.n_tiers - 1].item0 + P.w[TP.n_tiers - 1].n_items;
+  if (items == 0) return CSAQ_OK;
+  P.n_items_total = items;
+  P.slot_bytes = pl.slot_bytes;
+  P.depth = pl.depth;
+  P.want2 = pl.want2;
+  P.x_bytes = pl.x_bytes;
+  // the grid depends on the shapes and the SM count only (never on M)
+  int ctas = (items + kWarps - 1) / kWarps;
+  ctas = ctas < grid_ctas_max() ? ctas : grid_ctas_max();
+  P.n_warps = ctas * kWarps;
+  partition(TP, P.w, K, P.n_warps, P.begin);
+  qgemv_mma_kernel<ACT, NT><<<(unsigned)ctas, kThreads, pl.smem_bytes, st>>>(P, K, x, M, ldx);
   return launch_status();
 }
 
 template <typename ACT>
 int launch_mma(const TierParams& P0, int64_t K, const void* x, int64_t M, int64_t ldx,
-               cudaStream_t st) {
+               void* workspace, cudaStream_t st) {
   if (P0.tile_start[P0.n_tiers] == 0) return CSAQ_OK;
   int64_t m0 = 0;
   while (m0 < M) {
-    // as many tokens (<= 16) as the shared-memory plan allows
     int mb = (int)((M - m0) < 16 ? (M - m0) : 16);
-    LaunchCfg probe;
-    while (mb > 1 && !plan(K, mb, mb > 8 ? 2 : 1, probe)) --mb;
+    Plan probe;
+    while (mb > 1 && !make_plan(P0, K, mb, probe)) --mb;
     TierParams P = P0;
     for (int i = 0; i < P.n_tiers; ++i) {
       P.t[i].y = reinterpret_cast<ACT*>(P.t[i].y) + m0 * P.t[i].ldy;
@@ -770,8 +1075,8 @@ int launch_mma(const TierParams& P0, int64_t K, const void* x, int64_t M, int64_
         P.t[i].residual = reinterpret_cast<const ACT*>(P.t[i].residual) + m0 * P.t[i].ldr;
     }
     const ACT* xb = reinterpret_cast<const ACT*>(x) + m0 * ldx;
-    const int rc = mb <= 8 ? launch_mma_block<ACT, 1>(P, K, xb, mb, ldx, st)
-                           : launch_mma_block<ACT, 2>(P, K, xb, mb, ldx, st);
+    const int rc = mb <= 8 ? launch_mma_block<ACT, 1>(P, K, xb, mb, ldx, workspace, st)
+                           : launch_mma_block<ACT, 2>(P, K, xb, mb, ldx, workspace, st);
     if (rc) return rc;
     m0 += mb;
   }
@@ -800,7 +1105,8 @@ extern "C" int64_t csaq_tile_blocks_bytes(int bits, int64_t n_rows, int64_t K) {
   if ((bits != 2 && bits != 4 && bits != 8 && bits != 16) || n_rows < 0 || K <= 0 || K % 128)
     return -1;
   const int64_t tiles = (n_rows + kTileRows - 1) / kTileRows;
-  return tiles * (K / 128) * block_bytes(bits);
+  const int64_t units = (tiles + unit_tiles(bits) - 1) / unit_tiles(bits);
+  return units * (K / 128) * chunk_bytes(bits);
 }
 
 extern "C" int csaq_repack_tiles(const csaq_tier* tier, int64_t K, uint8_t* blocks, void* stream) {
@@ -817,28 +1123,38 @@ extern "C" int csaq_repack_tiles(const csaq_tier* tier, int64_t K, uint8_t* bloc
   if (T.n_rows == 0) return CSAQ_OK;
   cudaStream_t st = as_stream(stream);
   const int64_t n_chunks = K / 128;
-  const int64_t n_tiles = (T.n_rows + kTileRows - 1) / kTileRows;
+  const int64_t tiles = (T.n_rows + kTileRows - 1) / kTileRows;
+  const int64_t units = (tiles + unit_tiles(T.bits) - 1) / unit_tiles(T.bits);
   const int piece = T.bits == 2 ? 8 : 16;
-  const int64_t pieces = n_tiles * n_chunks * 2 * (4 * T.bits / piece) * 32;
-  repack_codes_kernel<<<(pieces + 255) / 256, 256, 0, st>>>(T, n_chunks, T.bits, n_tiles, blocks);
+  const int64_t pieces = units * n_chunks * unit_tiles(T.bits) * (code_bytes(T.bits) / piece);
+  repack_codes_kernel<<<(pieces + 255) / 256, 256, 0, st>>>(T, n_chunks, units, blocks);
   int rc = launch_status();
   if (rc || T.bits == 16) return rc;
-  const int64_t metas = n_tiles * n_chunks * kTileRows;
-  repack_meta_kernel<<<(metas + 255) / 256, 256, 0, st>>>(T, n_chunks, T.bits, n_tiles, blocks);
+  const int64_t metas = units * n_chunks * unit_tiles(T.bits) * kTileRows;
+  repack_meta_kernel<<<(metas + 255) / 256, 256, 0, st>>>(T, n_chunks, units, blocks);
   return launch_status();
 }
 
+extern "C" int64_t csaq_qgemv_workspace_bytes(const csaq_tier* tiers, int n_tiers, int64_t K) {
+  TierParams P;
+  if (build_params(tiers, n_tiers, K, P)) return -1;
+  return workspace_layout(P, K, nullptr, nullptr);
+}
+
 extern "C" int csaq_qgemv(const csaq_tier* tiers, int n_tiers, int64_t K, const void* x,
-                          int x_dtype, int64_t M, int64_t ldx, void* stream) {
+                          int x_dtype, int64_t M, int64_t ldx, void* workspace,
+                          int64_t workspace_bytes, void* stream) {
   TierParams P;
   int rc = build_params(tiers, n_tiers, K, P);
   if (rc) return rc;
   if (!x || M < 0 || ldx < K || !dtype_size(x_dtype)) return CSAQ_ERR_ARG;
   if (M == 0) return CSAQ_OK;
   cudaStream_t st = as_stream(stream);
-  if (x_dtype != CSAQ_DT_F32 && mma_eligible(P, K, x, ldx)) {
-    return x_dtype == CSAQ_DT_BF16 ? launch_mma<__nv_bfloat16>(P, K, x, M, ldx, st)
-                                   : launch_mma<__half>(P, K, x, M, ldx, st);
+  if (x_dtype != CSAQ_DT_F32 && mma_eligible(P, K, x, ldx) && workspace &&
+      workspace_bytes >= workspace_layout(P, K, nullptr, nullptr) &&
+      reinterpret_cast<uintptr_t>(workspace) % 16 == 0) {
+    return x_dtype == CSAQ_DT_BF16 ? launch_mma<__nv_bfloat16>(P, K, x, M, ldx, workspace, st)
+                                   : launch_mma<__half>(P, K, x, M, ldx, workspace, st);
   }
   if (!simt_eligible(P)) return CSAQ_ERR_UNSUPPORTED;
   if (x_dtype == CSAQ_DT_F32) return launch_simt<float>(P, K, x, M, ldx, st);
@@ -858,4 +1174,12 @@ extern "C" int csaq_qgemv_simt(const csaq_tier* tiers, int n_tiers, int64_t K, c
   if (x_dtype == CSAQ_DT_F32) return launch_simt<float>(P, K, x, M, ldx, st);
   return x_dtype == CSAQ_DT_BF16 ? launch_simt<__nv_bfloat16>(P, K, x, M, ldx, st)
                                  : launch_simt<__half>(P, K, x, M, ldx, st);
+}
+
+extern "C" int csaq_qgemv_wait_timeouts(int64_t* count) {
+  if (!count) return CSAQ_ERR_ARG;
+  unsigned int v = 0;
+  if (cudaMemcpyFromSymbol(&v, g_wait_timeouts, sizeof(v)) != cudaSuccess) return launch_status();
+  *count = v;
+  return CSAQ_OK;
 }

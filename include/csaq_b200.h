@@ -141,11 +141,22 @@ int csaq_repack_tiles(const csaq_tier* tier, int64_t K, uint8_t* blocks, void* s
 /* y[m, out_rows[i]] = residual + sum_k W[i, k] * x[m, k] + bias, fp32
  * accumulation; x is M x ldx in x_dtype (F32, F16 or BF16), y and bias and
  * residual in the same dtype. F16/BF16 use the tensor-core kernel when every
- * tier with rows has `blocks` (csaq_repack_tiles) and x is 16-byte aligned
- * with ldx % 8 == 0; everything else (and F32) uses the CUDA-core kernel,
- * which reads the reference layout (`codes`, `scales`, `zps`). */
+ * tier with rows has `blocks` (csaq_repack_tiles), x is 16-byte aligned with
+ * ldx % 8 == 0 and a workspace of csaq_qgemv_workspace_bytes is given; that
+ * workspace (16-byte aligned) must be zero before its first use, is left zero
+ * by every completed call, and must not be shared by calls that can run at the
+ * same time. Everything else (and F32) uses the CUDA-core kernel, which reads
+ * the reference layout (`codes`, `scales`, `zps`). Results of the tensor-core
+ * kernel for one token do not depend on M. */
+int64_t csaq_qgemv_workspace_bytes(const csaq_tier* tiers, int n_tiers, int64_t K);
 int csaq_qgemv(const csaq_tier* tiers, int n_tiers, int64_t K, const void* x, int x_dtype,
-               int64_t M, int64_t ldx, void* stream);
+               int64_t M, int64_t ldx, void* workspace, int64_t workspace_bytes, void* stream);
+
+/* Number of warps, since the library was loaded on this device, whose bounded
+ * wait for a weight copy in the tensor-core kernel gave up (the launch still
+ * ends; its output is then unreliable). Synchronises the device. No
+ * counterpart in the reference (its kernels have no device-side waits). */
+int csaq_qgemv_wait_timeouts(int64_t* count);
 
 /* Same contract, always the CUDA-core kernel (any K, any group size, any M);
  * a second GPU path used to cross-check the tensor-core kernel. */

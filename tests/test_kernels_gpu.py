@@ -247,11 +247,14 @@ def test_qgemv_tensor_core_vs_cuda_core():
     layer, case, _ = _mixed_layer(300, 1024, seed=5, dtype=torch.bfloat16, bits=(16, 8, 4, 2))
     x = torch.randn(7, 1024, generator=torch.Generator().manual_seed(9)).to(torch.bfloat16).to(DEV)
     ys = []
-    for fn in (lib().csaq_qgemv, lib().csaq_qgemv_simt):
+    for simt in (False, True):
         y = torch.zeros(7, 300, dtype=torch.bfloat16, device=DEV)
         d = layer.gemv_descriptors(y)
-        check(fn(_lib.tier_array(d), len(d), 1024, x.data_ptr(), dtype_code(x.dtype), 7, 1024,
-                 stream_of(x)), "qgemv")
+        if simt:
+            check(lib().csaq_qgemv_simt(_lib.tier_array(d), len(d), 1024, x.data_ptr(), dtype_code(x.dtype), 7,
+                                        1024, stream_of(x)), "qgemv")
+        else:
+            _lib.qgemv(d, 1024, x, 7, _lib.Workspace())
         ys.append(y.float().cpu().numpy())
     assert_linear_close(ys[0], ys[1], what="mma vs simt")
 
@@ -286,8 +289,7 @@ def test_qgemv_residual_fusion():
     r = torch.randn(3, 128, generator=torch.Generator().manual_seed(2)).to(torch.bfloat16).to(DEV)
     y = r.clone()
     d = layer.gemv_descriptors(y, residual=y)
-    check(lib().csaq_qgemv(_lib.tier_array(d), len(d), 256, x.data_ptr(), dtype_code(x.dtype), 3,
-                           256, stream_of(x)), "qgemv")
+    _lib.qgemv(d, 256, x, 3, _lib.Workspace())
     ref = r.float() + layer(x).float()
     assert_linear_close(y.float().cpu().numpy(), ref.cpu().numpy(), what="residual")
 
@@ -300,6 +302,45 @@ def test_qgemv_full_size_mixed_linear():
         x = torch.randn(m, 4096, generator=torch.Generator().manual_seed(m)).half()
         y = layer(x.to(DEV)).float().cpu().numpy()
         assert_linear_close(y, O.linear_ref(x.float().numpy(), Wref), what=f"4096 m={m}")
+
+
+@pytest.mark.parametrize("shape", [(4096, 4096), (1024, 14336), (300, 512)])
+def test_qgemv_token_result_independent_of_m(shape):
+    """A token's output is bitwise the same whether it is launched alone or
+    with other tokens (the work partition does not depend on M)."""
+    n, k = shape
+    layer, _, _ = _mixed_layer(n, k, seed=3, dtype=torch.bfloat16)
+    x = torch.randn(13, k, generator=torch.Generator().manual_seed(5)).to(torch.bfloat16).to(DEV)
+    y_all = layer(x)
+    for m in (1, 5, 13):
+        y_m = layer(x[:m])
+        assert torch.equal(y_m, y_all[:m]), m
+
+
+def test_qgemv_workspace_shared_across_shapes():
+    """One workspace serves launches of different layer shapes in stream order."""
+    from csaq import _lib
+    a, _, _ = _mixed_layer(4096, 1024, seed=1, dtype=torch.bfloat16)
+    b, _, _ = _mixed_layer(512, 4096, seed=2, dtype=torch.bfloat16, bits=(8, 4, 2))
+    xa = torch.randn(3, 1024, generator=torch.Generator().manual_seed(1)).to(torch.bfloat16).to(DEV)
+    xb = torch.randn(3, 4096, generator=torch.Generator().manual_seed(2)).to(torch.bfloat16).to(DEV)
+    ref_a, ref_b = a(xa), b(xb)
+    ws = _lib.Workspace()
+    for _ in range(3):
+        ya = torch.empty_like(ref_a)
+        yb = torch.empty_like(ref_b)
+        _lib.qgemv(a.gemv_descriptors(ya), 1024, xa, 3, ws)
+        _lib.qgemv(b.gemv_descriptors(yb), 4096, xb, 3, ws)
+        assert torch.equal(ya, ref_a) and torch.equal(yb, ref_b)
+
+
+def test_qgemv_no_abandoned_waits():
+    """After the GEMV tests above, no warp gave up waiting for a weight copy."""
+    import ctypes
+    from csaq._lib import check, lib
+    n = ctypes.c_int64(-1)
+    check(lib().csaq_qgemv_wait_timeouts(ctypes.byref(n)), "wait_timeouts")
+    assert n.value == 0
 
 
 def test_uniform_layer_ragged_shapes():
