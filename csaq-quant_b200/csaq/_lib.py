@@ -66,6 +66,7 @@ _SIGNATURES = {
     "csaq_dequant": (c_int, [c_vp, c_vp, c_vp, c_int, c_i64, c_i64, c_i64, c_int, c_int, c_vp, c_vp]),
     "csaq_qgemv_workspace_bytes": (c_i64, [ctypes.POINTER(CsaqTier), c_int, c_i64]),
     "csaq_qgemv_wait_timeouts": (c_int, [ctypes.POINTER(c_i64)]),
+    "csaq_qgemv_static": (c_int, [ctypes.POINTER(CsaqTier), c_int, c_i64, c_vp, c_int, c_i64, c_i64, c_vp]),
     "csaq_qgemv": (c_int, [ctypes.POINTER(CsaqTier), c_int, c_i64, c_vp, c_int, c_i64, c_i64, c_vp, c_i64,
                            c_vp]),
     "csaq_qgemv_simt": (c_int, [ctypes.POINTER(CsaqTier), c_int, c_i64, c_vp, c_int, c_i64, c_i64, c_vp]),

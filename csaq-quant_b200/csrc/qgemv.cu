@@ -1183,3 +1183,59 @@ extern "C" int csaq_qgemv_wait_timeouts(int64_t* count) {
   *count = v;
   return CSAQ_OK;
 }
+
+// ── csaq_qgemv_static: the GEMV with library-owned scratch ──────────────────
+// For callers with no device allocator of their own (see the header). The
+// scratch holds what csaq_qgemv's workspace holds: per-CTA sums of cut units
+// and the unit tickets, which must start at zero and which every completed
+// launch leaves at zero.
+static __device__ __align__(256) uint8_t g_static_scratch[CSAQ_QGEMV_STATIC_SCRATCH_BYTES];
+
+namespace csaq {
+namespace {
+constexpr int kMaxDevices = 64;
+std::mutex g_static_mu;
+void* g_static_ptr[kMaxDevices];
+
+// Once per device, with that device current: the buffer's address, zero-filled.
+int static_scratch(void** out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) {
+    set_last_cuda_error(e);
+    return CSAQ_ERR_CUDA;
+  }
+  if (dev < 0 || dev >= kMaxDevices) return CSAQ_ERR_UNSUPPORTED;
+  std::lock_guard<std::mutex> lock(g_static_mu);
+  if (!g_static_ptr[dev]) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_static_scratch);
+    if (e == cudaSuccess) e = cudaMemset(p, 0, CSAQ_QGEMV_STATIC_SCRATCH_BYTES);
+    if (e == cudaSuccess) e = cudaDeviceSynchronize();
+    if (e != cudaSuccess) {
+      set_last_cuda_error(e);
+      return CSAQ_ERR_CUDA;
+    }
+    g_static_ptr[dev] = p;
+  }
+  *out = g_static_ptr[dev];
+  return CSAQ_OK;
+}
+}  // namespace
+}  // namespace csaq
+
+extern "C" int csaq_qgemv_static(const csaq_tier* tiers, int n_tiers, int64_t K, const void* x,
+                                 int x_dtype, int64_t M, int64_t ldx, void* stream) {
+  TierParams P;
+  const int rc = build_params(tiers, n_tiers, K, P);
+  if (rc) return rc;
+  if (!x || M < 0 || ldx < K || !dtype_size(x_dtype)) return CSAQ_ERR_ARG;
+  const int64_t need = workspace_layout(P, K, nullptr, nullptr);
+  if (need < 0 || need > CSAQ_QGEMV_STATIC_SCRATCH_BYTES) return CSAQ_ERR_SCRATCH;
+  if (M == 0) return CSAQ_OK;
+  void* scratch = nullptr;
+  const int src = static_scratch(&scratch);
+  if (src) return src;
+  return csaq_qgemv(tiers, n_tiers, K, x, x_dtype, M, ldx, scratch, CSAQ_QGEMV_STATIC_SCRATCH_BYTES,
+                    stream);
+}

@@ -30,6 +30,7 @@ enum {
   CSAQ_ERR_CUDA = -3,         /* a CUDA launch failed; see csaq_last_cuda_error */
   CSAQ_ERR_TIMEOUT = -4,      /* a bounded device wait gave up                  */
   CSAQ_ERR_UNSUPPORTED = -5,  /* shape/alignment outside what the kernel serves */
+  CSAQ_ERR_SCRATCH = -6,      /* the launch needs more scratch than csaq_qgemv_static holds */
 };
 
 enum { CSAQ_DT_F32 = 0, CSAQ_DT_F16 = 1, CSAQ_DT_BF16 = 2 };
@@ -157,6 +158,24 @@ int csaq_qgemv(const csaq_tier* tiers, int n_tiers, int64_t K, const void* x, in
  * ends; its output is then unreliable). Synchronises the device. No
  * counterpart in the reference (its kernels have no device-side waits). */
 int csaq_qgemv_wait_timeouts(int64_t* count);
+
+/* csaq_qgemv for callers that cannot allocate device memory: a host-language
+ * binding that is handed raw device pointers by an application owning all
+ * device memory, or a latency-critical caller for which cudaMalloc/cudaFree
+ * (which may synchronise the device) are not acceptable. No counterpart in
+ * the reference (its linear allocates through PyTorch).
+ *
+ * Same arguments and results as csaq_qgemv minus the workspace: the scratch
+ * is a fixed CSAQ_QGEMV_STATIC_SCRATCH_BYTES buffer inside the library, one
+ * per device. A launch whose csaq_qgemv_workspace_bytes exceeds it returns
+ * CSAQ_ERR_SCRATCH before anything is enqueued. The first call on each device
+ * sets the buffer up (looks up its address and zero-fills it, synchronously);
+ * make that first call before any stream capture. Calls on one device share
+ * the buffer, so calls that can overlap on the GPU (other streams, other host
+ * threads) race; calls ordered on one stream do not. */
+#define CSAQ_QGEMV_STATIC_SCRATCH_BYTES (1 << 20)
+int csaq_qgemv_static(const csaq_tier* tiers, int n_tiers, int64_t K, const void* x, int x_dtype,
+                      int64_t M, int64_t ldx, void* stream);
 
 /* Same contract, always the CUDA-core kernel (any K, any group size, any M);
  * a second GPU path used to cross-check the tensor-core kernel. */
