@@ -64,11 +64,8 @@ _SIGNATURES = {
     "csaq_unpack": (c_int, [c_vp, c_int, c_i64, c_i64, c_vp, c_vp]),
     "csaq_float_to_int": (c_int, [c_vp, c_vp, c_vp, c_int, c_i64, c_i64, c_vp, c_vp]),
     "csaq_dequant": (c_int, [c_vp, c_vp, c_vp, c_int, c_i64, c_i64, c_i64, c_int, c_int, c_vp, c_vp]),
-    "csaq_qgemv_workspace_bytes": (c_i64, [ctypes.POINTER(CsaqTier), c_int, c_i64]),
     "csaq_qgemv_wait_timeouts": (c_int, [ctypes.POINTER(c_i64)]),
-    "csaq_qgemv_static": (c_int, [ctypes.POINTER(CsaqTier), c_int, c_i64, c_vp, c_int, c_i64, c_i64, c_vp]),
-    "csaq_qgemv": (c_int, [ctypes.POINTER(CsaqTier), c_int, c_i64, c_vp, c_int, c_i64, c_i64, c_vp, c_i64,
-                           c_vp]),
+    "csaq_qgemv": (c_int, [ctypes.POINTER(CsaqTier), c_int, c_i64, c_vp, c_int, c_i64, c_i64, c_vp]),
     "csaq_qgemv_simt": (c_int, [ctypes.POINTER(CsaqTier), c_int, c_i64, c_vp, c_int, c_i64, c_i64, c_vp]),
     "csaq_tile_blocks_bytes": (c_i64, [c_int, c_i64, c_i64]),
     "csaq_repack_tiles": (c_int, [ctypes.POINTER(CsaqTier), c_i64, c_vp, c_vp]),
@@ -85,6 +82,8 @@ _SIGNATURES = {
     "csaq_attention_workspace_floats": (c_i64, [c_i64, c_i64, c_i64, c_i64, c_i64, c_i64]),
     "csaq_decode_attention": (c_int, [c_vp, c_vp, c_vp, c_vp, c_i64, c_i64, c_i64, c_i64, c_i64, c_i64,
                                       ctypes.c_float, c_vp, c_vp, c_vp, c_int, c_vp]),
+    "csaq_decode_attention_static": (c_int, [c_vp, c_vp, c_vp, c_vp, c_i64, c_i64, c_i64, c_i64, c_i64, c_i64,
+                                             ctypes.c_float, c_vp, c_int, c_vp]),
     "csaq_silu_mul": (c_int, [c_vp, c_i64, c_vp, c_i64, c_vp, c_i64, c_i64, c_i64, c_int, c_vp]),
     "csaq_spec_accept": (c_int, [c_vp, c_vp, c_i64, c_i64, c_vp, c_vp, c_vp, c_i64, c_vp, c_vp, c_vp, c_vp, c_vp]),
     "csaq_greedy_commit": (c_int, [c_vp, c_i64, c_vp, c_vp, c_vp, c_i64, c_vp, c_vp, c_vp]),
@@ -176,43 +175,8 @@ def tier_array(tiers: Sequence[CsaqTier]):
     return arr
 
 
-class Workspace:
-    """Zero-initialised device scratch for csaq_qgemv (grows on demand; every
-    completed launch leaves its tickets at zero, so it is zeroed only when
-    reallocated). Launches that may run concurrently need separate ones."""
-
-    def __init__(self):
-        self.buf = None
-
-    def get(self, nbytes: int, device) -> torch.Tensor:
-        nbytes = max(int(nbytes), 16)
-        if self.buf is None or self.buf.numel() < nbytes or self.buf.device != torch.device(device):
-            self.buf = torch.zeros((nbytes + 15) // 16 * 16, dtype=torch.uint8, device=device)
-        return self.buf
-
-
-_SHARED_WS: dict = {}
-
-
-def shared_workspace(device, stream: int) -> Workspace:
-    """One workspace per (device, stream): launches on one stream are ordered."""
-    key = (str(torch.device(device)), int(stream or 0))
-    ws = _SHARED_WS.get(key)
-    if ws is None:
-        ws = _SHARED_WS[key] = Workspace()
-    return ws
-
-
-def qgemv(descs, K: int, x: torch.Tensor, M: int, ws: "Workspace" = None, stream: int = None) -> None:
-    """Launch csaq_qgemv on ctypes descriptors with a workspace from `ws`
-    (default: the shared workspace of x's device and the stream)."""
-    L = lib()
+def qgemv(descs, K: int, x: torch.Tensor, M: int, stream: int = None) -> None:
+    """Launch csaq_qgemv on a list of ctypes tier descriptors."""
     arr = tier_array(descs) if isinstance(descs, list) else descs
-    n = len(descs)
     st = stream if stream is not None else stream_of(x)
-    if ws is None:
-        ws = shared_workspace(x.device, st)
-    need = L.csaq_qgemv_workspace_bytes(arr, n, K)
-    buf = ws.get(need if need > 0 else 16, x.device)
-    check(L.csaq_qgemv(arr, n, K, x.data_ptr(), dtype_code(x.dtype), M, x.stride(0), buf.data_ptr(),
-                       buf.numel(), st), "qgemv")
+    check(lib().csaq_qgemv(arr, len(descs), K, x.data_ptr(), dtype_code(x.dtype), M, x.stride(0), st), "qgemv")

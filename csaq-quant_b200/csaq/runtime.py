@@ -132,7 +132,6 @@ class DecodeRuntime:
         self.n_out = torch.zeros(B, dtype=i32, device=self.dev)
         self.argmax_buf = torch.zeros(B * (lookahead + 1), dtype=i64, device=self.dev)
         self.shapes: Dict[int, _Shape] = {}
-        self.workspace = torch.zeros(16, dtype=torch.uint8, device=self.dev)
         self.graphs: Dict[str, torch.cuda.CUDAGraph] = {}
         self.launches_per_step: Dict[str, int] = {}
 
@@ -179,15 +178,6 @@ class DecodeRuntime:
                     sh.descs[(li, name, verify)] = (_lib.tier_array(d), len(d))
         d = self.lm_head.gemv_descriptors(sh.logits)
         sh.descs[("lm", "all")] = (_lib.tier_array(d), len(d))
-        # one zeroed workspace serves every GEMV of the runtime (they run in stream order)
-        need = 16
-        for (key, (arr, n)) in sh.descs.items():
-            K = self.I if (len(key) == 3 and key[1] == "down") else (
-                self.Hq * self.D if (len(key) == 3 and key[1] == "o") else self.H)
-            need = max(need, lib().csaq_qgemv_workspace_bytes(arr, n, K))
-        if need > self.workspace.numel():
-            self.workspace = torch.zeros((need + 15) // 16 * 16, dtype=torch.uint8, device=self.dev)
-            self.graphs.clear()  # captured graphs hold the old workspace pointer
         d = self.lm_head.gemv_descriptors(sh.logits[: self.B])
         sh.descs[("lm", "last")] = (_lib.tier_array(d), len(d))
         self.shapes[S] = sh
@@ -196,9 +186,7 @@ class DecodeRuntime:
     # ── one step of S tokens per sequence ───────────────────────────────────
     def _gemv(self, arr_n, K: int, x: torch.Tensor, M: int, st: int) -> None:
         arr, n = arr_n
-        ws = self.workspace
-        check(lib().csaq_qgemv(arr, n, K, x.data_ptr(), self.dt, M, x.stride(0), ws.data_ptr(), ws.numel(),
-                               st), "qgemv")
+        check(lib().csaq_qgemv(arr, n, K, x.data_ptr(), self.dt, M, x.stride(0), st), "qgemv")
 
     @torch.no_grad()
     def step(self, S: int, ids: torch.Tensor, pos: torch.Tensor, verify: bool,
@@ -241,9 +229,7 @@ class DecodeRuntime:
         if last_only and S > 1:
             arr, n = sh.descs[("lm", "last")]
             last = sh.xn[S - 1:]  # rows S-1, 2S-1, ...: the last token of each sequence
-            ws = self.workspace
-            check(L.csaq_qgemv(arr, n, H, last.data_ptr(), self.dt, self.B, S * H, ws.data_ptr(), ws.numel(), st),
-                  "lm_head")
+            check(L.csaq_qgemv(arr, n, H, last.data_ptr(), self.dt, self.B, S * H, st), "lm_head")
             return sh.logits[: self.B]
         self._gemv(sh.descs[("lm", "all")], H, sh.xn, M, st)
         return sh.logits

@@ -18,7 +18,7 @@ extern "C" const char* csaq_status_string(int status) {
     case CSAQ_ERR_CUDA: return "CUDA launch failed";
     case CSAQ_ERR_TIMEOUT: return "bounded device wait timed out";
     case CSAQ_ERR_UNSUPPORTED: return "shape or alignment not supported by this kernel";
-    case CSAQ_ERR_SCRATCH: return "launch needs more scratch than the static buffer of csaq_qgemv_static holds";
+    case CSAQ_ERR_SCRATCH: return "call needs more scratch than the static buffer of csaq_decode_attention_static holds";
     default: return "unknown status";
   }
 }

@@ -13,14 +13,17 @@
 //     fp16 rows are stored pre-arranged in the 4-bit column order (values in
 //     "high" positions times 16, exact).
 //   * Work = (unit, chunk) items of every tier of the launch, spread over the
-//     warps of a one-CTA-per-SM grid as contiguous ranges of equal byte cost
-//     (stream-K). Each warp streams its blocks through a cp.async ring in
-//     shared memory. A unit whose chunks all fall in one warp's range is
-//     finished in registers; a unit cut by a range boundary gets one partial
-//     sum per warp in the workspace and a ticket, and the warp completing it
-//     adds the partials in warp order. The partition depends only on the tier
-//     shapes and the SM count, so a token's result is bitwise independent of
-//     how many tokens share the launch.
+//     warps of a one-CTA-per-SM grid of 2-CTA clusters: each cluster takes a
+//     run of whole units, cut so the clusters carry equal block bytes, and
+//     each of its 32 warps an equal-cost run of items (stream-K). Each warp
+//     streams its blocks into a shared-memory ring by bulk copies. A unit
+//     whose chunks all fall in one warp's range is finished in registers; a
+//     unit cut between warps leaves one partial sum per warp in shared
+//     memory, and after a cluster barrier the highest of those warps adds
+//     them in warp order, reading the other CTA's through distributed shared
+//     memory. The partition depends only on the tier shapes and the SM count,
+//     so a token's result is bitwise independent of how many tokens share the
+//     launch.
 //   * Activations are staged once per CTA as fp16 MMA B-fragments ("records"),
 //     scaled per token by a power of two (exact for bf16 / fp16 inputs).
 //   * Codes become fp16 MMA operands with one LOP3 per register: a nibble
@@ -37,6 +40,7 @@
 
 #include <algorithm>
 #include <mutex>
+#include <type_traits>
 #include <vector>
 
 #include "common.cuh"
@@ -312,7 +316,6 @@ struct TierWork {
   int bits, mt, n_units;
   int item0;    // first item of the tier
   int n_items;  // n_units * n_chunks
-  int ticket0;  // first ticket (one per unit)
 };
 
 struct KParams {
@@ -324,8 +327,6 @@ struct KParams {
   int depth;       // ring slots per warp
   int want2;       // any 2-bit tier (stage R2 records)
   int x_bytes;     // R4 records: n_chunks * M * kRecStride (R2 the same again when want2)
-  float* contrib;  // [cta][2][32 rows x 16 tokens] sums of units cut by a CTA boundary
-  int* tickets;    // [unit] chunks done so far (zero between launches)
   int begin[kMaxWarps + 1];
 };
 
@@ -392,12 +393,31 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
   return false;
 }
 
+// ── thread-block cluster helpers (distributed shared memory) ────────────────
+constexpr int kCluster = 2;  // CTAs per cluster: a unit's partial sums never leave its cluster
+
+__device__ __forceinline__ void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+// the shared::cluster address of `saddr` (a local shared address) in CTA `rank` of the cluster
+__device__ __forceinline__ uint32_t dsmem_addr(uint32_t saddr, int rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(saddr), "r"(rank));
+  return r;
+}
+__device__ __forceinline__ float ld_dsmem_f32(uint32_t addr) {
+  float v;
+  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(addr) : "memory");
+  return v;
+}
+
 // One 128-column chunk of one unit: acc[tile][n-tile][fragment] += the chunk's
 // contribution (see the header comment for the algebra).
-template <int NT>
-__device__ __forceinline__ void chunk_math(int bits, const uint8_t* slot, const uint8_t* rbase,
+template <int BITS, int NT>
+__device__ __forceinline__ void chunk_math(const uint8_t* slot, const uint8_t* rbase,
                                            const float4* xcs_ch, int M, int lane,
                                            float (&acc)[2][NT][4]) {
+  constexpr int bits = BITS;
   const int g = lane >> 2, c = lane & 3;
 #pragma unroll
   for (int nt = 0; nt < NT; ++nt) {
@@ -414,7 +434,7 @@ __device__ __forceinline__ void chunk_math(int bits, const uint8_t* slot, const 
     const int t0 = nt * 8 + 2 * c;
     const float4 cs0 = t0 < M ? xcs_ch[t0] : make_float4(0.f, 0.f, 0.f, 0.f);
     const float4 cs1 = t0 + 1 < M ? xcs_ch[t0 + 1] : make_float4(0.f, 0.f, 0.f, 0.f);
-    if (bits == 4 || bits == 8) {
+    if constexpr (bits == 4 || bits == 8) {
       // 4-bit: [tile][h][word]; 8-bit: [nibble plane][h][word] of one tile
       uint32_t cw[2][2][4];
       float gg[2][2][4];
@@ -431,7 +451,7 @@ __device__ __forceinline__ void chunk_math(int bits, const uint8_t* slot, const 
         for (int a = 0; a < 2; ++a) gg[mt][a][0] = gg[mt][a][1] = gg[mt][a][2] = gg[mt][a][3] = 0.0f;
       }
       mma4(cw, rec, gg);
-      if (bits == 4) {
+      if constexpr (bits == 4) {
 #pragma unroll
         for (int mt = 0; mt < 2; ++mt) {
           const uint8_t* meta = slot + mt * tile_block_bytes(4) + code_bytes(4);
@@ -460,7 +480,7 @@ __device__ __forceinline__ void chunk_math(int bits, const uint8_t* slot, const 
         acc[0][nt][2] = fmaf(s1, fmaf(-z1, cs0.y, d[2]), acc[0][nt][2]);
         acc[0][nt][3] = fmaf(s1, fmaf(-z1, cs1.y, d[3]), acc[0][nt][3]);
       }
-    } else if (bits == 16) {
+    } else if constexpr (bits == 16) {
       uint32_t cw[2][16];
       float gg[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
       const uint4* cp = reinterpret_cast<const uint4*>(slot);
@@ -515,7 +535,8 @@ struct UnitRef {
 };
 
 template <typename ACT, int NT>
-__global__ void __launch_bounds__(kThreads, 1) qgemv_mma_kernel(const __grid_constant__ KParams P,
+__global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kThreads, 1)
+    qgemv_mma_kernel(const __grid_constant__ KParams P,
                                                                 int64_t K, const ACT* __restrict__ x,
                                                                 int M, int64_t ldx) {
   extern __shared__ __align__(16) uint8_t smem[];
@@ -533,8 +554,6 @@ __global__ void __launch_bounds__(kThreads, 1) qgemv_mma_kernel(const __grid_con
   const int wg = blockIdx.x * kWarps + warp;
   const int it_begin = P.begin[wg];
   const int it_end = P.begin[wg + 1];
-  const int cta_begin = P.begin[blockIdx.x * kWarps];
-  const int cta_end = P.begin[(blockIdx.x + 1) * kWarps];
 
   if (lane == 0) {
     for (int s = 0; s < P.depth; ++s) mbar_init(&bars[s], 1);
@@ -572,14 +591,17 @@ __global__ void __launch_bounds__(kThreads, 1) qgemv_mma_kernel(const __grid_con
   if (threadIdx.x < 16) smax[threadIdx.x] = 0u;
   __syncthreads();
   const int k8 = (int)(K / 8);
-  for (int u = threadIdx.x; u < M * k8; u += blockDim.x) {
-    const int tok = u / k8, kk = u - tok * k8;
-    const uint4 q = ld_cached_v4(x + (int64_t)tok * ldx + 8 * kk);
-    const ACT* e = reinterpret_cast<const ACT*>(&q);
+  for (int tok = 0; tok < M; ++tok) {
     float mx = 0.0f;
+    for (int kk = threadIdx.x; kk < k8; kk += blockDim.x) {
+      const uint4 q = ld_cached_v4(x + (int64_t)tok * ldx + 8 * kk);
+      const ACT* e = reinterpret_cast<const ACT*>(&q);
 #pragma unroll
-    for (int j = 0; j < 8; ++j) mx = fmaxf(mx, fabsf(to_f32<ACT>(e[j])));
-    atomicMax(&smax[tok], __float_as_uint(mx));
+      for (int j = 0; j < 8; ++j) mx = fmaxf(mx, fabsf(to_f32<ACT>(e[j])));
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    if (lane == 0 && mx > 0.0f) atomicMax(&smax[tok], __float_as_uint(mx));
   }
   __syncthreads();
   if (threadIdx.x < 16) {
@@ -622,7 +644,8 @@ __global__ void __launch_bounds__(kThreads, 1) qgemv_mma_kernel(const __grid_con
 
   // ── main loop over the warp's units ──────────────────────────────────────
   float acc[2][NT][4], fst[2][NT][4];
-  UnitRef split[2] = {{-1, 0, 0, 0}, {-1, 0, 0, 0}};  // [0]: first unit, [1]: last unit (when cut)
+  // cut units of this warp: [0] its first unit, [1] its last one (tier -1: none)
+  int cut_t0 = -1, cut_u0 = 0, cut_s0 = 0, cut_t1 = -1, cut_u1 = 0, cut_s1 = 0;
   uint32_t phase = 0;                                  // parity bit per ring slot
   uint32_t late = 0, late_parity = 0;                 // slots whose wait was abandoned
   int c_slot = 0;
@@ -631,6 +654,21 @@ __global__ void __launch_bounds__(kThreads, 1) qgemv_mma_kernel(const __grid_con
     t = tier_of_item(P, item);
     local = item - P.w[t].item0;
   }
+  auto chunks = [&](auto bits_c, int ch_first, int ch_last) {
+    constexpr int B = decltype(bits_c)::value;
+    for (int ch = ch_first; ch < ch_last; ++ch) {
+      if (!mbar_wait(&bars[c_slot], (phase >> c_slot) & 1u)) {
+        late |= 1u << c_slot;
+        late_parity = (late_parity & ~(1u << c_slot)) | (phase & (1u << c_slot));
+      }
+      phase ^= 1u << c_slot;
+      chunk_math<B, NT>(ring + c_slot * P.slot_bytes, (B == 2 ? rec2 : rec4) + (int64_t)ch * M * kRecStride,
+                        xcs + ch * M, M, lane, acc);
+      __syncwarp();
+      issue();
+      c_slot = (c_slot + 1 == P.depth) ? 0 : c_slot + 1;
+    }
+  };
   while (item < it_end) {
     const TierWork& tw = P.w[t];
     const csaq_tier& T = P.tp.t[t];
@@ -642,18 +680,11 @@ __global__ void __launch_bounds__(kThreads, 1) qgemv_mma_kernel(const __grid_con
     for (int a = 0; a < 2; ++a)
 #pragma unroll
       for (int nt = 0; nt < NT; ++nt) acc[a][nt][0] = acc[a][nt][1] = acc[a][nt][2] = acc[a][nt][3] = 0.0f;
-
-    for (int ch = ch_first; ch < ch_last; ++ch) {
-      if (!mbar_wait(&bars[c_slot], (phase >> c_slot) & 1u)) {
-        late |= 1u << c_slot;
-        late_parity = (late_parity & ~(1u << c_slot)) | (phase & (1u << c_slot));
-      }
-      phase ^= 1u << c_slot;
-      chunk_math<NT>(tw.bits, ring + c_slot * P.slot_bytes,
-                     (tw.bits == 2 ? rec2 : rec4) + (int64_t)ch * M * kRecStride, xcs + ch * M, M, lane, acc);
-      __syncwarp();
-      issue();
-      c_slot = (c_slot + 1 == P.depth) ? 0 : c_slot + 1;
+    switch (tw.bits) {
+      case 4: chunks(std::integral_constant<int, 4>(), ch_first, ch_last); break;
+      case 8: chunks(std::integral_constant<int, 8>(), ch_first, ch_last); break;
+      case 16: chunks(std::integral_constant<int, 16>(), ch_first, ch_last); break;
+      default: chunks(std::integral_constant<int, 2>(), ch_first, ch_last); break;
     }
 
     const int u_start = tw.item0 + unit * n_chunks;
@@ -669,7 +700,7 @@ __global__ void __launch_bounds__(kThreads, 1) qgemv_mma_kernel(const __grid_con
             if (mt < tw.mt && tok < M && row < T.n_rows) store_out<ACT>(T, row, tok, acc[mt][nt][e], xexp[tok]);
           }
     } else if (item == it_begin) {
-      split[0] = {t, unit, u_start, u_start + n_chunks};
+      cut_t0 = t; cut_u0 = unit; cut_s0 = u_start;
 #pragma unroll
       for (int a = 0; a < 2; ++a)
 #pragma unroll
@@ -677,7 +708,7 @@ __global__ void __launch_bounds__(kThreads, 1) qgemv_mma_kernel(const __grid_con
 #pragma unroll
           for (int e = 0; e < 4; ++e) fst[a][nt][e] = acc[a][nt][e];
     } else {
-      split[1] = {t, unit, u_start, u_start + n_chunks};  // the last unit: stays in acc
+      cut_t1 = t; cut_u1 = unit; cut_s1 = u_start;  // the last unit: stays in acc
     }
 
     item += ch_last - ch_first;
@@ -694,12 +725,13 @@ __global__ void __launch_bounds__(kThreads, 1) qgemv_mma_kernel(const __grid_con
       if (late & (1u << s)) mbar_wait(&bars[s], (late_parity >> s) & 1u);
   }
 
-  // ── cut units: partials of the CTA's warps meet in shared memory ──────────
-  __syncthreads();  // every ring is drained
+  // ── cut units: partials of the cluster's warps meet in distributed shared memory
+  __syncthreads();  // every ring of this CTA is drained
   float* part = reinterpret_cast<float*>(ring_all);  // [warp][2][32 rows][M]
 #pragma unroll
   for (int s = 0; s < 2; ++s) {
-    if (split[s].t < 0) continue;
+    const int ct = s == 0 ? cut_t0 : cut_t1;
+    if (ct < 0) continue;
     float* dst = part + (warp * 2 + s) * 32 * M;
 #pragma unroll
     for (int mt = 0; mt < 2; ++mt)
@@ -708,85 +740,49 @@ __global__ void __launch_bounds__(kThreads, 1) qgemv_mma_kernel(const __grid_con
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
           const int tok = frag_tok(nt, e, lane);
-          if (mt < P.w[split[s].t].mt && tok < M)
+          if (mt < P.w[ct].mt && tok < M)
             dst[frag_row(mt, e, lane) * M + tok] = s == 0 ? fst[mt][nt][e] : acc[mt][nt][e];
         }
   }
-  __syncthreads();
+  cluster_sync();  // partials of both CTAs written and visible
 
+  const uint32_t part_sa = smem_u32(part);
 #pragma unroll 1
   for (int s = 0; s < 2; ++s) {
-    const UnitRef u = split[s];
-    if (u.t < 0) continue;
-    // the highest warp of this CTA holding part of the unit reduces it
-    if (P.begin[wg + 1] < min(u.end, cta_end)) continue;
-    const TierWork& tw = P.w[u.t];
-    const csaq_tier& T = P.tp.t[u.t];
+    const int ut = s == 0 ? cut_t0 : cut_t1;
+    if (ut < 0) continue;
+    const int unit = s == 0 ? cut_u0 : cut_u1;
+    const int u_start = s == 0 ? cut_s0 : cut_s1, u_end = u_start + n_chunks;
+    // units never cross a cluster boundary; the highest warp holding part of
+    // the unit adds the partials in warp order and writes y
+    if (P.begin[wg + 1] < u_end) continue;
+    const TierWork& tw = P.w[ut];
+    const csaq_tier& T = P.tp.t[ut];
     const int rows = tw.mt * kTileRows;
     const int n_val = rows * M, nv = (n_val + 31) >> 5;  // values per lane: e = lane + 32 j
     float v[16];
 #pragma unroll
     for (int j = 0; j < 16; ++j) v[j] = 0.0f;
-    const int w0 = warp_of_item(P, max(u.start, cta_begin));
-    for (int w = w0; w <= wg; ++w) {
+    for (int w = warp_of_item(P, u_start); w <= wg; ++w) {
       const int b = P.begin[w];
       if (b == P.begin[w + 1]) continue;  // empty range
-      const float* src = part + ((w - blockIdx.x * kWarps) * 2 + (b >= u.start ? 0 : 1)) * 32 * M;
+      const uint32_t off = (uint32_t)((((w % kWarps) * 2 + (b >= u_start ? 0 : 1)) * 32 * M) * 4);
+      const uint32_t src = dsmem_addr(part_sa + off, (w / kWarps) % kCluster);
 #pragma unroll
       for (int j = 0; j < 16; ++j) {
         if (j >= nv) break;
         const int e = lane + 32 * j;
-        if (e < n_val) v[j] += src[e];
-      }
-    }
-    if (u.start >= cta_begin && u.end <= cta_end) {
-#pragma unroll
-      for (int j = 0; j < 16; ++j) {
-        if (j >= nv) break;
-        const int e = lane + 32 * j, r = e / M, tok = e - r * M, row = u.unit * rows + r;
-        if (e < n_val && row < T.n_rows) store_out<ACT>(T, row, tok, v[j], xexp[tok]);
-      }
-      continue;
-    }
-    // the unit crosses a CTA boundary: publish this CTA's sum, take a ticket;
-    // the CTA completing the unit adds the CTA sums in CTA order
-    float* gdst = P.contrib + ((int64_t)blockIdx.x * 2 + (cta_begin >= u.start ? 0 : 1)) * (32 * 16);
-#pragma unroll
-    for (int j = 0; j < 16; ++j) {
-      if (j >= nv) break;
-      const int e = lane + 32 * j;
-      if (e < n_val) __stcg(gdst + e, v[j]);
-    }
-    __threadfence();
-    __syncwarp();
-    const int done = min(u.end, cta_end) - max(u.start, cta_begin);
-    int old = 0;
-    if (lane == 0) old = atomicAdd(P.tickets + tw.ticket0 + u.unit, done);
-    old = __shfl_sync(0xffffffffu, old, 0);
-    if (old + done != n_chunks) continue;
-    __threadfence();
-#pragma unroll
-    for (int j = 0; j < 16; ++j) v[j] = 0.0f;
-    for (int cta = warp_of_item(P, u.start) / kWarps; cta < (int)gridDim.x; ++cta) {
-      const int b = P.begin[cta * kWarps];
-      if (b >= u.end) break;
-      if (b == P.begin[(cta + 1) * kWarps]) continue;  // empty CTA
-      const float* src = P.contrib + ((int64_t)cta * 2 + (b >= u.start ? 0 : 1)) * (32 * 16);
-#pragma unroll
-      for (int j = 0; j < 16; ++j) {
-        if (j >= nv) break;
-        const int e = lane + 32 * j;
-        if (e < n_val) v[j] += __ldcg(src + e);
+        if (e < n_val) v[j] += ld_dsmem_f32(src + 4u * (uint32_t)e);
       }
     }
 #pragma unroll
     for (int j = 0; j < 16; ++j) {
       if (j >= nv) break;
-      const int e = lane + 32 * j, r = e / M, tok = e - r * M, row = u.unit * rows + r;
+      const int e = lane + 32 * j, r = e / M, tok = e - r * M, row = unit * rows + r;
       if (e < n_val && row < T.n_rows) store_out<ACT>(T, row, tok, v[j], xexp[tok]);
     }
-    if (lane == 0) P.tickets[tw.ticket0 + u.unit] = 0;  // ready for the next launch
   }
+  cluster_sync();  // no CTA leaves while the other may still read its partials
 }
 
 // ── CUDA-core reference kernel ──────────────────────────────────────────────
@@ -897,41 +893,38 @@ int num_sms() {
 
 constexpr int kSmemBudget = 227 * 1024;
 constexpr int kRingBudget = 12 * 1024;  // bytes of weights in flight per warp (target)
-constexpr int kContribFloats = 2 * 32 * 16;  // per CTA: two units x 32 rows x 16 tokens
 
-int grid_ctas_max() { return num_sms() < kMaxCtas ? num_sms() : kMaxCtas; }
+// CTAs of the grid at most: the SM count, capped, a multiple of the cluster size
+int grid_ctas_max() {
+  const int n = num_sms() < kMaxCtas ? num_sms() : kMaxCtas;
+  return n / kCluster * kCluster > 0 ? n / kCluster * kCluster : kCluster;
+}
 
-// Workspace: per-CTA sums of units cut by a CTA boundary (a fixed region for a
-// given device, so launches of different shapes can share one workspace), then
-// one ticket per unit of every tier, in tier order. Returns -1 when the launch has
-// more work items than the kernel indexes.
-int64_t workspace_layout(const TierParams& TP, int64_t K, TierWork* w, int64_t* tickets_off) {
+// Fill the per-tier work table; -1 when the launch has more work items than
+// the kernel indexes.
+int64_t work_table(const TierParams& TP, int64_t K, TierWork* w) {
   const int64_t n_chunks = K / 128;
-  const int64_t contrib = (int64_t)grid_ctas_max() * kContribFloats * 4;
-  int64_t tk = 0, items = 0;
+  int64_t items = 0;
   for (int i = 0; i < TP.n_tiers; ++i) {
     const csaq_tier& t = TP.t[i];
     const int mt = unit_tiles(t.bits);
     const int64_t tiles = ((int64_t)t.n_rows + kTileRows - 1) / kTileRows;
     const int64_t units = (tiles + mt - 1) / mt;
-    if (w) {
-      w[i].bits = t.bits;
-      w[i].mt = mt;
-      w[i].n_units = (int)units;
-      w[i].item0 = (int)items;
-      w[i].n_items = (int)(units * n_chunks);
-      w[i].ticket0 = (int)tk;
-    }
-    tk += units;
+    w[i].bits = t.bits;
+    w[i].mt = mt;
+    w[i].n_units = (int)units;
+    w[i].item0 = (int)items;
+    w[i].n_items = (int)(units * n_chunks);
     items += units * n_chunks;
   }
-  if (items >= (int64_t)1 << 30) return -1;
-  if (tickets_off) *tickets_off = contrib;
-  return contrib + tk * 4;
+  return items >= (int64_t)1 << 30 ? -1 : items;
 }
 
-// Cut the items into W runs of equal block bytes: warp w starts at the first
-// item whose start cost is >= floor(C w / W). Cached per shape.
+// The partition, cached per shape. Cluster j (kCluster CTAs) takes the units
+// between two unit boundaries, chosen nearest to the cost targets C j / G, so
+// that no unit leaves its cluster; inside a cluster its kCluster * kWarps
+// warps take runs of equal cost, cut at chunk granularity (item start cost >=
+// the warp's target). Costs are block bytes / 16.
 struct PartitionCache {
   struct Entry {
     std::vector<int> key;
@@ -959,27 +952,53 @@ bool partition(const TierParams& TP, const TierWork* w, int64_t K, int n_warps, 
       std::copy(e.begin.begin(), e.begin.end(), begin);
       return true;
     }
-  int64_t total = 0;
-  for (int i = 0; i < TP.n_tiers; ++i) total += (int64_t)(chunk_bytes(w[i].bits) / 16) * w[i].n_items;
-  std::vector<int> b(n_warps + 1);
-  int t = 0;
-  int64_t cost0 = 0;  // cost before tier t
-  for (int k = 0; k <= n_warps; ++k) {
-    const int64_t target = total * k / n_warps;
-    while (t < TP.n_tiers && cost0 + (int64_t)(chunk_bytes(w[t].bits) / 16) * w[t].n_items <= target) {
-      cost0 += (int64_t)(chunk_bytes(w[t].bits) / 16) * w[t].n_items;
-      ++t;
-    }
-    if (t == TP.n_tiers || k == n_warps) {
-      b[k] = w[TP.n_tiers - 1].item0 + w[TP.n_tiers - 1].n_items;
-      continue;
-    }
-    const int64_t ic = chunk_bytes(w[t].bits) / 16;
-    const int64_t d = target - cost0;
-    int64_t i = d <= 0 ? 0 : (d + ic - 1) / ic;
-    if (i > w[t].n_items) i = w[t].n_items;
-    b[k] = w[t].item0 + (int)i;
+  const int n_tiers = TP.n_tiers;
+  const int64_t n_chunks = K / 128;
+  std::vector<int64_t> ic(n_tiers), cost0(n_tiers + 1);
+  cost0[0] = 0;
+  for (int i = 0; i < n_tiers; ++i) {
+    ic[i] = chunk_bytes(w[i].bits) / 16;
+    cost0[i + 1] = cost0[i] + ic[i] * w[i].n_items;
   }
+  const int64_t total = cost0[n_tiers];
+  const int n_items = w[n_tiers - 1].item0 + w[n_tiers - 1].n_items;
+  auto cost_at = [&](int item) -> int64_t {  // start cost of an item (or the end)
+    int t = 0;
+    while (t + 1 < n_tiers && item >= w[t + 1].item0) ++t;
+    return cost0[t] + ic[t] * (item - w[t].item0);
+  };
+  // first item whose start cost is >= target, within [lo, hi]
+  auto first_at = [&](int64_t target, int lo, int hi) -> int {
+    while (lo < hi) {
+      const int mid = lo + (hi - lo) / 2;
+      if (cost_at(mid) >= target) hi = mid; else lo = mid + 1;
+    }
+    return lo;
+  };
+  const int n_clusters = n_warps / (kWarps * kCluster);
+  const int per_cluster = kWarps * kCluster;
+  std::vector<int> cb(n_clusters + 1);
+  cb[0] = 0;
+  cb[n_clusters] = n_items;
+  for (int j = 1; j < n_clusters; ++j) {
+    const int64_t target = total * j / n_clusters;
+    int t = 0;
+    while (t + 1 < n_tiers && target >= cost0[t + 1]) ++t;
+    const int64_t unit_cost = ic[t] * n_chunks;
+    int64_t u = unit_cost > 0 ? (target - cost0[t] + unit_cost / 2) / unit_cost : 0;
+    if (u > w[t].n_units) u = w[t].n_units;
+    int item = w[t].item0 + (int)(u * n_chunks);
+    if (item < cb[j - 1]) item = cb[j - 1];
+    if (item > n_items) item = n_items;
+    cb[j] = item;
+  }
+  std::vector<int> b(n_warps + 1);
+  for (int j = 0; j < n_clusters; ++j) {
+    const int64_t c0 = cost_at(cb[j]), c1 = cost_at(cb[j + 1]);
+    for (int k = 0; k < per_cluster; ++k)
+      b[j * per_cluster + k] = k == 0 ? cb[j] : first_at(c0 + (c1 - c0) * k / per_cluster, cb[j], cb[j + 1]);
+  }
+  b[n_warps] = n_items;
   std::copy(b.begin(), b.end(), begin);
   if (cache.entries.size() < 64) {
     cache.entries.push_back({key, b});
@@ -1031,18 +1050,14 @@ int set_smem_attr() {
 }
 
 template <typename ACT, int NT>
-int launch_mma_block(const TierParams& TP, int64_t K, const ACT* x, int M, int64_t ldx,
-                     void* workspace, cudaStream_t st) {
+int launch_mma_block(const TierParams& TP, int64_t K, const ACT* x, int M, int64_t ldx, cudaStream_t st) {
   Plan pl;
   if (!make_plan(TP, K, M, pl)) return CSAQ_ERR_UNSUPPORTED;
   int rc = set_smem_attr<ACT, NT>();
   if (rc) return rc;
   static thread_local KParams P;  // about 12 KB: kept off the stack
   P.tp = TP;
-  int64_t tick_off = 0;
-  if (workspace_layout(TP, K, P.w, &tick_off) < 0) return CSAQ_ERR_UNSUPPORTED;
-  P.contrib = reinterpret_cast<float*>(workspace);
-  P.tickets = reinterpret_cast<int*>(reinterpret_cast<uint8_t*>(workspace) + tick_off);
+  if (work_table(TP, K, P.w) < 0) return CSAQ_ERR_UNSUPPORTED;
   const int items = P.w[TP.n_tiers - 1].item0 + P.w[TP.n_tiers - 1].n_items;
   if (items == 0) return CSAQ_OK;
   P.n_items_total = items;
@@ -1052,6 +1067,7 @@ int launch_mma_block(const TierParams& TP, int64_t K, const ACT* x, int M, int64
   P.x_bytes = pl.x_bytes;
   // the grid depends on the shapes and the SM count only (never on M)
   int ctas = (items + kWarps - 1) / kWarps;
+  ctas = (ctas + kCluster - 1) / kCluster * kCluster;
   ctas = ctas < grid_ctas_max() ? ctas : grid_ctas_max();
   P.n_warps = ctas * kWarps;
   partition(TP, P.w, K, P.n_warps, P.begin);
@@ -1060,8 +1076,7 @@ int launch_mma_block(const TierParams& TP, int64_t K, const ACT* x, int M, int64
 }
 
 template <typename ACT>
-int launch_mma(const TierParams& P0, int64_t K, const void* x, int64_t M, int64_t ldx,
-               void* workspace, cudaStream_t st) {
+int launch_mma(const TierParams& P0, int64_t K, const void* x, int64_t M, int64_t ldx, cudaStream_t st) {
   if (P0.tile_start[P0.n_tiers] == 0) return CSAQ_OK;
   int64_t m0 = 0;
   while (m0 < M) {
@@ -1075,8 +1090,8 @@ int launch_mma(const TierParams& P0, int64_t K, const void* x, int64_t M, int64_
         P.t[i].residual = reinterpret_cast<const ACT*>(P.t[i].residual) + m0 * P.t[i].ldr;
     }
     const ACT* xb = reinterpret_cast<const ACT*>(x) + m0 * ldx;
-    const int rc = mb <= 8 ? launch_mma_block<ACT, 1>(P, K, xb, mb, ldx, workspace, st)
-                           : launch_mma_block<ACT, 2>(P, K, xb, mb, ldx, workspace, st);
+    const int rc = mb <= 8 ? launch_mma_block<ACT, 1>(P, K, xb, mb, ldx, st)
+                           : launch_mma_block<ACT, 2>(P, K, xb, mb, ldx, st);
     if (rc) return rc;
     m0 += mb;
   }
@@ -1135,26 +1150,17 @@ extern "C" int csaq_repack_tiles(const csaq_tier* tier, int64_t K, uint8_t* bloc
   return launch_status();
 }
 
-extern "C" int64_t csaq_qgemv_workspace_bytes(const csaq_tier* tiers, int n_tiers, int64_t K) {
-  TierParams P;
-  if (build_params(tiers, n_tiers, K, P)) return -1;
-  return workspace_layout(P, K, nullptr, nullptr);
-}
-
 extern "C" int csaq_qgemv(const csaq_tier* tiers, int n_tiers, int64_t K, const void* x,
-                          int x_dtype, int64_t M, int64_t ldx, void* workspace,
-                          int64_t workspace_bytes, void* stream) {
+                          int x_dtype, int64_t M, int64_t ldx, void* stream) {
   TierParams P;
   int rc = build_params(tiers, n_tiers, K, P);
   if (rc) return rc;
   if (!x || M < 0 || ldx < K || !dtype_size(x_dtype)) return CSAQ_ERR_ARG;
   if (M == 0) return CSAQ_OK;
   cudaStream_t st = as_stream(stream);
-  if (x_dtype != CSAQ_DT_F32 && mma_eligible(P, K, x, ldx) && workspace &&
-      workspace_bytes >= workspace_layout(P, K, nullptr, nullptr) &&
-      reinterpret_cast<uintptr_t>(workspace) % 16 == 0) {
-    return x_dtype == CSAQ_DT_BF16 ? launch_mma<__nv_bfloat16>(P, K, x, M, ldx, workspace, st)
-                                   : launch_mma<__half>(P, K, x, M, ldx, workspace, st);
+  if (x_dtype != CSAQ_DT_F32 && mma_eligible(P, K, x, ldx)) {
+    return x_dtype == CSAQ_DT_BF16 ? launch_mma<__nv_bfloat16>(P, K, x, M, ldx, st)
+                                   : launch_mma<__half>(P, K, x, M, ldx, st);
   }
   if (!simt_eligible(P)) return CSAQ_ERR_UNSUPPORTED;
   if (x_dtype == CSAQ_DT_F32) return launch_simt<float>(P, K, x, M, ldx, st);
@@ -1182,60 +1188,4 @@ extern "C" int csaq_qgemv_wait_timeouts(int64_t* count) {
   if (cudaMemcpyFromSymbol(&v, g_wait_timeouts, sizeof(v)) != cudaSuccess) return launch_status();
   *count = v;
   return CSAQ_OK;
-}
-
-// ── csaq_qgemv_static: the GEMV with library-owned scratch ──────────────────
-// For callers with no device allocator of their own (see the header). The
-// scratch holds what csaq_qgemv's workspace holds: per-CTA sums of cut units
-// and the unit tickets, which must start at zero and which every completed
-// launch leaves at zero.
-static __device__ __align__(256) uint8_t g_static_scratch[CSAQ_QGEMV_STATIC_SCRATCH_BYTES];
-
-namespace csaq {
-namespace {
-constexpr int kMaxDevices = 64;
-std::mutex g_static_mu;
-void* g_static_ptr[kMaxDevices];
-
-// Once per device, with that device current: the buffer's address, zero-filled.
-int static_scratch(void** out) {
-  int dev = 0;
-  cudaError_t e = cudaGetDevice(&dev);
-  if (e != cudaSuccess) {
-    set_last_cuda_error(e);
-    return CSAQ_ERR_CUDA;
-  }
-  if (dev < 0 || dev >= kMaxDevices) return CSAQ_ERR_UNSUPPORTED;
-  std::lock_guard<std::mutex> lock(g_static_mu);
-  if (!g_static_ptr[dev]) {
-    void* p = nullptr;
-    e = cudaGetSymbolAddress(&p, g_static_scratch);
-    if (e == cudaSuccess) e = cudaMemset(p, 0, CSAQ_QGEMV_STATIC_SCRATCH_BYTES);
-    if (e == cudaSuccess) e = cudaDeviceSynchronize();
-    if (e != cudaSuccess) {
-      set_last_cuda_error(e);
-      return CSAQ_ERR_CUDA;
-    }
-    g_static_ptr[dev] = p;
-  }
-  *out = g_static_ptr[dev];
-  return CSAQ_OK;
-}
-}  // namespace
-}  // namespace csaq
-
-extern "C" int csaq_qgemv_static(const csaq_tier* tiers, int n_tiers, int64_t K, const void* x,
-                                 int x_dtype, int64_t M, int64_t ldx, void* stream) {
-  TierParams P;
-  const int rc = build_params(tiers, n_tiers, K, P);
-  if (rc) return rc;
-  if (!x || M < 0 || ldx < K || !dtype_size(x_dtype)) return CSAQ_ERR_ARG;
-  const int64_t need = workspace_layout(P, K, nullptr, nullptr);
-  if (need < 0 || need > CSAQ_QGEMV_STATIC_SCRATCH_BYTES) return CSAQ_ERR_SCRATCH;
-  if (M == 0) return CSAQ_OK;
-  void* scratch = nullptr;
-  const int src = static_scratch(&scratch);
-  if (src) return src;
-  return csaq_qgemv(tiers, n_tiers, K, x, x_dtype, M, ldx, scratch, CSAQ_QGEMV_STATIC_SCRATCH_BYTES,
-                    stream);
 }

@@ -7,6 +7,8 @@
 // KV cache (B, Hkv, Lmax, D); per-sequence start positions pos0[B] (the
 // position of the step's first token). Token (b, s) sits at position pos0[b]+s.
 
+#include <mutex>
+
 #include "common.cuh"
 
 namespace csaq {
@@ -333,4 +335,63 @@ extern "C" int csaq_greedy_commit(const int64_t* tok, int64_t B, int32_t* pos0, 
   commit_kernel<<<blocks_for(B, 128), 128, 0, as_stream(stream)>>>(tok, (int)B, pos0, out_tokens, n_out,
                                                                   (int)cap, next_tok, remaining);
   return launch_status();
+}
+
+// ── csaq_decode_attention_static: decode attention with library-owned scratch
+// For callers with no device allocator of their own (see the header). The
+// scratch holds what csaq_decode_attention's `part` and `tickets` hold: the
+// per-chunk partial softmax results (rewritten by every call) and one ticket
+// per (sequence, KV head), which must start at zero and which every completed
+// call leaves at zero.
+static __device__ __align__(256) uint8_t g_attn_scratch[CSAQ_ATTENTION_STATIC_SCRATCH_BYTES];
+
+namespace csaq {
+namespace {
+constexpr int kMaxDevices = 64;
+std::mutex g_attn_mu;
+void* g_attn_ptr[kMaxDevices];
+
+// Once per device, with that device current: the buffer's address, zero-filled.
+int attn_scratch(void** out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) {
+    set_last_cuda_error(e);
+    return CSAQ_ERR_CUDA;
+  }
+  if (dev < 0 || dev >= kMaxDevices) return CSAQ_ERR_UNSUPPORTED;
+  std::lock_guard<std::mutex> lock(g_attn_mu);
+  if (!g_attn_ptr[dev]) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_attn_scratch);
+    if (e == cudaSuccess) e = cudaMemset(p, 0, CSAQ_ATTENTION_STATIC_SCRATCH_BYTES);
+    if (e == cudaSuccess) e = cudaDeviceSynchronize();
+    if (e != cudaSuccess) {
+      set_last_cuda_error(e);
+      return CSAQ_ERR_CUDA;
+    }
+    g_attn_ptr[dev] = p;
+  }
+  *out = g_attn_ptr[dev];
+  return CSAQ_OK;
+}
+}  // namespace
+}  // namespace csaq
+
+extern "C" int csaq_decode_attention_static(const void* q, const void* k_cache, const void* v_cache,
+                                            const int32_t* pos0, int64_t B, int64_t S, int64_t Hq,
+                                            int64_t Hkv, int64_t D, int64_t Lmax, float scale, void* out,
+                                            int dtype, void* stream) {
+  if (!q || !k_cache || !v_cache || !pos0 || !out) return CSAQ_ERR_ARG;
+  const int64_t floats = csaq_attention_workspace_floats(B, S, Hq, Hkv, D, Lmax);
+  if (floats < 0) return CSAQ_ERR_ARG;
+  const int64_t part_bytes = (floats * 4 + 255) / 256 * 256;
+  if (part_bytes + B * Hkv * 4 > CSAQ_ATTENTION_STATIC_SCRATCH_BYTES) return CSAQ_ERR_SCRATCH;
+  void* scratch = nullptr;
+  const int rc = attn_scratch(&scratch);
+  if (rc) return rc;
+  float* part = reinterpret_cast<float*>(scratch);
+  int32_t* tickets = reinterpret_cast<int32_t*>(reinterpret_cast<uint8_t*>(scratch) + part_bytes);
+  return csaq_decode_attention(q, k_cache, v_cache, pos0, B, S, Hq, Hkv, D, Lmax, scale, part, tickets, out,
+                               dtype, stream);
 }

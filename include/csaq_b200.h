@@ -30,7 +30,7 @@ enum {
   CSAQ_ERR_CUDA = -3,         /* a CUDA launch failed; see csaq_last_cuda_error */
   CSAQ_ERR_TIMEOUT = -4,      /* a bounded device wait gave up                  */
   CSAQ_ERR_UNSUPPORTED = -5,  /* shape/alignment outside what the kernel serves */
-  CSAQ_ERR_SCRATCH = -6,      /* the launch needs more scratch than csaq_qgemv_static holds */
+  CSAQ_ERR_SCRATCH = -6,      /* the call needs more scratch than csaq_decode_attention_static holds */
 };
 
 enum { CSAQ_DT_F32 = 0, CSAQ_DT_F16 = 1, CSAQ_DT_BF16 = 2 };
@@ -142,40 +142,18 @@ int csaq_repack_tiles(const csaq_tier* tier, int64_t K, uint8_t* blocks, void* s
 /* y[m, out_rows[i]] = residual + sum_k W[i, k] * x[m, k] + bias, fp32
  * accumulation; x is M x ldx in x_dtype (F32, F16 or BF16), y and bias and
  * residual in the same dtype. F16/BF16 use the tensor-core kernel when every
- * tier with rows has `blocks` (csaq_repack_tiles), x is 16-byte aligned with
- * ldx % 8 == 0 and a workspace of csaq_qgemv_workspace_bytes is given; that
- * workspace (16-byte aligned) must be zero before its first use, is left zero
- * by every completed call, and must not be shared by calls that can run at the
- * same time. Everything else (and F32) uses the CUDA-core kernel, which reads
- * the reference layout (`codes`, `scales`, `zps`). Results of the tensor-core
- * kernel for one token do not depend on M. */
-int64_t csaq_qgemv_workspace_bytes(const csaq_tier* tiers, int n_tiers, int64_t K);
+ * tier with rows has `blocks` (csaq_repack_tiles) and x is 16-byte aligned with
+ * ldx % 8 == 0; everything else (and F32) uses the CUDA-core kernel, which
+ * reads the reference layout (`codes`, `scales`, `zps`). Results of the
+ * tensor-core kernel for one token do not depend on M. */
 int csaq_qgemv(const csaq_tier* tiers, int n_tiers, int64_t K, const void* x, int x_dtype,
-               int64_t M, int64_t ldx, void* workspace, int64_t workspace_bytes, void* stream);
+               int64_t M, int64_t ldx, void* stream);
 
 /* Number of warps, since the library was loaded on this device, whose bounded
  * wait for a weight copy in the tensor-core kernel gave up (the launch still
  * ends; its output is then unreliable). Synchronises the device. No
  * counterpart in the reference (its kernels have no device-side waits). */
 int csaq_qgemv_wait_timeouts(int64_t* count);
-
-/* csaq_qgemv for callers that cannot allocate device memory: a host-language
- * binding that is handed raw device pointers by an application owning all
- * device memory, or a latency-critical caller for which cudaMalloc/cudaFree
- * (which may synchronise the device) are not acceptable. No counterpart in
- * the reference (its linear allocates through PyTorch).
- *
- * Same arguments and results as csaq_qgemv minus the workspace: the scratch
- * is a fixed CSAQ_QGEMV_STATIC_SCRATCH_BYTES buffer inside the library, one
- * per device. A launch whose csaq_qgemv_workspace_bytes exceeds it returns
- * CSAQ_ERR_SCRATCH before anything is enqueued. The first call on each device
- * sets the buffer up (looks up its address and zero-fills it, synchronously);
- * make that first call before any stream capture. Calls on one device share
- * the buffer, so calls that can overlap on the GPU (other streams, other host
- * threads) race; calls ordered on one stream do not. */
-#define CSAQ_QGEMV_STATIC_SCRATCH_BYTES (1 << 20)
-int csaq_qgemv_static(const csaq_tier* tiers, int n_tiers, int64_t K, const void* x, int x_dtype,
-                      int64_t M, int64_t ldx, void* stream);
 
 /* Same contract, always the CUDA-core kernel (any K, any group size, any M);
  * a second GPU path used to cross-check the tensor-core kernel. */
@@ -246,6 +224,27 @@ int csaq_decode_attention(const void* q, const void* k_cache, const void* v_cach
                           const int32_t* pos0, int64_t B, int64_t S, int64_t Hq, int64_t Hkv,
                           int64_t D, int64_t Lmax, float scale, float* part, int32_t* tickets,
                           void* out, int dtype, void* stream);
+
+/* csaq_decode_attention for callers that cannot allocate device memory: a
+ * host-language binding that is handed raw device pointers (q, the caches,
+ * pos0, out) by an application owning all device memory, or a
+ * latency-critical caller for which cudaMalloc/cudaFree (which may
+ * synchronise the device) are not acceptable. No counterpart in the reference
+ * (its attention is the HF module's, allocating through PyTorch).
+ *
+ * Same arguments and results as csaq_decode_attention minus `part` and
+ * `tickets`: those live in a fixed CSAQ_ATTENTION_STATIC_SCRATCH_BYTES buffer
+ * inside the library, one per device. A call needing more (partials of
+ * csaq_attention_workspace_floats floats, 256-byte aligned, then B*Hkv
+ * tickets) returns CSAQ_ERR_SCRATCH before anything is enqueued. The first
+ * call on each device sets the buffer up (looks up its address and zero-fills
+ * it, synchronously); make that first call before any stream capture. Calls
+ * on one device share the buffer, so calls that can overlap on the GPU (other
+ * streams, other host threads) race; calls ordered on one stream do not. */
+#define CSAQ_ATTENTION_STATIC_SCRATCH_BYTES (4 << 20)
+int csaq_decode_attention_static(const void* q, const void* k_cache, const void* v_cache,
+                                 const int32_t* pos0, int64_t B, int64_t S, int64_t Hq, int64_t Hkv,
+                                 int64_t D, int64_t Lmax, float scale, void* out, int dtype, void* stream);
 
 /* HF LlamaMLP gate: h = dtype(silu(g)) * u. */
 int csaq_silu_mul(const void* g, int64_t ldg, const void* u, int64_t ldu, void* h, int64_t ldh,

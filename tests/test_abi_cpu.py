@@ -70,9 +70,9 @@ def test_argument_validation_without_launch():
     assert L.csaq_dequant(dummy, None, None, 4, 4, 4, -1, 0, 0, dummy, None) == -1
     t = _lib.CsaqTier(bits=3, n_rows=1, group_size=128, n_groups=1, row_bytes=64)
     arr = _lib.tier_array([t])
-    assert L.csaq_qgemv(arr, 1, 128, dummy, 2, 1, 128, None, 0, None) == -2
-    assert L.csaq_qgemv(arr, 0, 128, dummy, 2, 1, 128, None, 0, None) == -1
-    assert L.csaq_qgemv(arr, 17, 128, dummy, 2, 1, 128, None, 0, None) == -1
+    assert L.csaq_qgemv(arr, 1, 128, dummy, 2, 1, 128, None) == -2
+    assert L.csaq_qgemv(arr, 0, 128, dummy, 2, 1, 128, None) == -1
+    assert L.csaq_qgemv(arr, 17, 128, dummy, 2, 1, 128, None) == -1
 
 
 def test_kernels_fail_loudly_without_cuda():

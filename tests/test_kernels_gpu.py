@@ -254,7 +254,7 @@ def test_qgemv_tensor_core_vs_cuda_core():
             check(lib().csaq_qgemv_simt(_lib.tier_array(d), len(d), 1024, x.data_ptr(), dtype_code(x.dtype), 7,
                                         1024, stream_of(x)), "qgemv")
         else:
-            _lib.qgemv(d, 1024, x, 7, _lib.Workspace())
+            _lib.qgemv(d, 1024, x, 7)
         ys.append(y.float().cpu().numpy())
     assert_linear_close(ys[0], ys[1], what="mma vs simt")
 
@@ -289,7 +289,7 @@ def test_qgemv_residual_fusion():
     r = torch.randn(3, 128, generator=torch.Generator().manual_seed(2)).to(torch.bfloat16).to(DEV)
     y = r.clone()
     d = layer.gemv_descriptors(y, residual=y)
-    _lib.qgemv(d, 256, x, 3, _lib.Workspace())
+    _lib.qgemv(d, 256, x, 3)
     ref = r.float() + layer(x).float()
     assert_linear_close(y.float().cpu().numpy(), ref.cpu().numpy(), what="residual")
 
@@ -315,23 +315,6 @@ def test_qgemv_token_result_independent_of_m(shape):
     for m in (1, 5, 13):
         y_m = layer(x[:m])
         assert torch.equal(y_m, y_all[:m]), m
-
-
-def test_qgemv_workspace_shared_across_shapes():
-    """One workspace serves launches of different layer shapes in stream order."""
-    from csaq import _lib
-    a, _, _ = _mixed_layer(4096, 1024, seed=1, dtype=torch.bfloat16)
-    b, _, _ = _mixed_layer(512, 4096, seed=2, dtype=torch.bfloat16, bits=(8, 4, 2))
-    xa = torch.randn(3, 1024, generator=torch.Generator().manual_seed(1)).to(torch.bfloat16).to(DEV)
-    xb = torch.randn(3, 4096, generator=torch.Generator().manual_seed(2)).to(torch.bfloat16).to(DEV)
-    ref_a, ref_b = a(xa), b(xb)
-    ws = _lib.Workspace()
-    for _ in range(3):
-        ya = torch.empty_like(ref_a)
-        yb = torch.empty_like(ref_b)
-        _lib.qgemv(a.gemv_descriptors(ya), 1024, xa, 3, ws)
-        _lib.qgemv(b.gemv_descriptors(yb), 4096, xb, 3, ws)
-        assert torch.equal(ya, ref_a) and torch.equal(yb, ref_b)
 
 
 def test_qgemv_no_abandoned_waits():
