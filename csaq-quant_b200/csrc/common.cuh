@@ -24,6 +24,43 @@ inline int launch_status() {
 
 inline cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s); }
 
+// ── programmatic dependent launch ──────────────────────────────────────────
+// A kernel started with launch_pdl may begin while its predecessor in the
+// stream is still running. pdl_wait() returns once the predecessor grid has
+// completed and its memory is visible; pdl_trigger() lets this grid's own
+// successor be scheduled. For a plain launch both are no-ops. Every kernel
+// launched this way calls pdl_wait() before it touches memory that another
+// kernel of the stream writes. Kernels that do not prefetch call pdl_trigger()
+// only after pdl_wait(), so at most one grid waits ahead of a running one and
+// waiting grids do not pile up on the SMs. CSAQ_PDL=0 in the environment turns
+// it off.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+bool pdl_enabled();
+
+template <typename... KArgs, typename... Args>
+inline int launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                      Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl_enabled() ? 1 : 0;
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
+  if (e != cudaSuccess) {
+    set_last_cuda_error(e);
+    (void)cudaGetLastError();
+    return CSAQ_ERR_CUDA;
+  }
+  return launch_status();
+}
+
 inline int dtype_size(int dt) {
   switch (dt) {
     case CSAQ_DT_F32: return 4;

@@ -1,9 +1,18 @@
 // Library identification, status strings and the per-thread CUDA error record.
+#include <cstdlib>
+
 #include "common.cuh"
 
 namespace csaq {
 static thread_local int g_last_cuda_error = 0;
 void set_last_cuda_error(cudaError_t e) { g_last_cuda_error = (int)e; }
+bool pdl_enabled() {
+  static const bool on = [] {
+    const char* v = getenv("CSAQ_PDL");
+    return !(v && v[0] == '0');
+  }();
+  return on;
+}
 }  // namespace csaq
 
 extern "C" const char* csaq_version(void) { return "csaq-b200 0.1.0 (sm_100a)"; }

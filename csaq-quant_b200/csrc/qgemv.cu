@@ -555,6 +555,7 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kThreads, 1)
   const int it_begin = P.begin[wg];
   const int it_end = P.begin[wg + 1];
 
+  pdl_trigger();
   if (lane == 0) {
     for (int s = 0; s < P.depth; ++s) mbar_init(&bars[s], 1);
     mbar_fence_init();
@@ -584,7 +585,8 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kThreads, 1)
       i_slot = (i_slot + 1 == P.depth) ? 0 : i_slot + 1;
     }
   };
-  for (int d = 0; d < P.depth; ++d) issue();  // weights first: they do not depend on x
+  for (int d = 0; d < P.depth; ++d) issue();  // weights first: no kernel writes them
+  pdl_wait();  // x (and y, bias, residual) may come from the previous kernel of the stream
 
   // token scales: e_t with max|x_t| * 2^-e_t in [2^14, 2^15)
   uint32_t* smax = reinterpret_cast<uint32_t*>(xexp);
@@ -800,6 +802,8 @@ __device__ __forceinline__ float weight_at(const csaq_tier& T, int row, int64_t 
 template <typename ACT>
 __global__ void qgemv_simt_kernel(const __grid_constant__ TierParams P, int64_t K,
                                   const ACT* __restrict__ x, int M, int64_t ldx, int row_blocks) {
+  pdl_wait();
+  pdl_trigger();
   const int lane = threadIdx.x & 31;
   const int64_t wid = (int64_t(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
   const int tok_blocks = (M + 7) / 8;
@@ -1071,8 +1075,8 @@ int launch_mma_block(const TierParams& TP, int64_t K, const ACT* x, int M, int64
   ctas = ctas < grid_ctas_max() ? ctas : grid_ctas_max();
   P.n_warps = ctas * kWarps;
   partition(TP, P.w, K, P.n_warps, P.begin);
-  qgemv_mma_kernel<ACT, NT><<<(unsigned)ctas, kThreads, pl.smem_bytes, st>>>(P, K, x, M, ldx);
-  return launch_status();
+  return launch_pdl(qgemv_mma_kernel<ACT, NT>, dim3((unsigned)ctas), dim3(kThreads), (size_t)pl.smem_bytes, st,
+                    P, K, x, M, ldx);
 }
 
 template <typename ACT>
@@ -1106,9 +1110,8 @@ int launch_simt(const TierParams& P, int64_t K, const void* x, int64_t M, int64_
   if (rows == 0) return CSAQ_OK;
   const int64_t warps = (int64_t)rows * ((M + 7) / 8);
   const int64_t blocks = (warps * 32 + 255) / 256;
-  qgemv_simt_kernel<ACT><<<blocks, 256, 0, st>>>(P, K, reinterpret_cast<const ACT*>(x), (int)M,
-                                                ldx, rows);
-  return launch_status();
+  return launch_pdl(qgemv_simt_kernel<ACT>, dim3((unsigned)blocks), dim3(256), 0, st, P, K,
+                    reinterpret_cast<const ACT*>(x), (int)M, ldx, rows);
 }
 
 }  // namespace

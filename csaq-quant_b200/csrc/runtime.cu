@@ -23,6 +23,8 @@ __device__ __forceinline__ float round_to(float v) {
 template <typename T>
 __global__ void rmsnorm_kernel(const T* __restrict__ x, int64_t ldx, const T* __restrict__ w,
                                T* __restrict__ y, int64_t ldy, int H, float eps) {
+  pdl_wait();
+  pdl_trigger();
   const int64_t row = blockIdx.x;
   const T* xr = x + row * ldx;
   __shared__ float red[32];
@@ -61,6 +63,8 @@ __global__ void rope_kv_kernel(const T* __restrict__ q, int64_t ldq, const T* __
                                const float* __restrict__ cos_t, const float* __restrict__ sin_t,
                                T* __restrict__ q_out, T* __restrict__ k_cache,
                                T* __restrict__ v_cache, int Lmax) {
+  pdl_wait();
+  pdl_trigger();
   const int64_t m = blockIdx.x;  // token
   const int b = (int)(m / S), s = (int)(m % S);
   const int pos = pos0[b] + s;
@@ -99,6 +103,8 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attention_kernel(
     const T* __restrict__ q, const T* __restrict__ k_cache, const T* __restrict__ v_cache,
     const int32_t* __restrict__ pos0, int S, int Hq, int Hkv, int Lmax, float scale,
     float* __restrict__ part, int32_t* __restrict__ tickets, T* __restrict__ out) {
+  pdl_wait();
+  pdl_trigger();
   constexpr int D = 128;
   const int bh = blockIdx.x, sp = blockIdx.y, n_split = gridDim.y;
   const int b = bh / Hkv, h = bh % Hkv;
@@ -179,6 +185,8 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attention_kernel(
 template <typename T>
 __global__ void silu_mul_kernel(const T* __restrict__ g, int64_t ldg, const T* __restrict__ u,
                                 int64_t ldu, T* __restrict__ h, int64_t ldh, int64_t M, int N) {
+  pdl_wait();
+  pdl_trigger();
   const int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
   if (i >= M * N) return;
   const int64_t m = i / N, n = i % N;
@@ -200,6 +208,8 @@ __global__ void accept_kernel(const int64_t* __restrict__ draft, const int64_t* 
                               int64_t* __restrict__ out_tokens, int32_t* __restrict__ n_out, int cap,
                               int64_t* __restrict__ next_tok, int32_t* __restrict__ n_new_out,
                               int64_t* __restrict__ stats, int32_t* __restrict__ remaining) {
+  pdl_wait();
+  pdl_trigger();
   const int b = blockIdx.x * blockDim.x + threadIdx.x;
   if (b >= B) return;
   int j = 0;
@@ -228,6 +238,8 @@ __global__ void accept_kernel(const int64_t* __restrict__ draft, const int64_t* 
 __global__ void commit_kernel(const int64_t* __restrict__ tok, int B, int32_t* __restrict__ pos0,
                               int64_t* __restrict__ out_tokens, int32_t* __restrict__ n_out, int cap,
                               int64_t* __restrict__ next_tok, int32_t* __restrict__ remaining) {
+  pdl_wait();
+  pdl_trigger();
   const int b = blockIdx.x * blockDim.x + threadIdx.x;
   if (b >= B) return;
   if (remaining[b] <= 0) return;  // a finished sequence stays put (cache bounds)
@@ -254,10 +266,9 @@ extern "C" int csaq_rmsnorm(const void* x, int64_t ldx, const void* w, void* y, 
   if (M == 0) return CSAQ_OK;
   cudaStream_t st = as_stream(stream);
   if (dtype == CSAQ_DT_BF16)
-    rmsnorm_kernel<__nv_bfloat16><<<M, 256, 0, st>>>((const __nv_bfloat16*)x, ldx, (const __nv_bfloat16*)w, (__nv_bfloat16*)y, ldy, (int)H, eps);
+    return launch_pdl(rmsnorm_kernel<__nv_bfloat16>, dim3(M), dim3(256), 0, st, (const __nv_bfloat16*)x, ldx, (const __nv_bfloat16*)w, (__nv_bfloat16*)y, ldy, (int)H, eps);
   else
-    rmsnorm_kernel<__half><<<M, 256, 0, st>>>((const __half*)x, ldx, (const __half*)w, (__half*)y, ldy, (int)H, eps);
-  return launch_status();
+    return launch_pdl(rmsnorm_kernel<__half>, dim3(M), dim3(256), 0, st, (const __half*)x, ldx, (const __half*)w, (__half*)y, ldy, (int)H, eps);
 }
 
 extern "C" int csaq_rope_kv(const void* q, int64_t ldq, const void* k, int64_t ldk, const void* v,
@@ -271,10 +282,9 @@ extern "C" int csaq_rope_kv(const void* q, int64_t ldq, const void* k, int64_t l
   cudaStream_t st = as_stream(stream);
   const int64_t M = B * S;
   if (dtype == CSAQ_DT_BF16)
-    rope_kv_kernel<__nv_bfloat16><<<M, 256, 0, st>>>((const __nv_bfloat16*)q, ldq, (const __nv_bfloat16*)k, ldk, (const __nv_bfloat16*)v, ldv, pos0, (int)S, (int)Hq, (int)Hkv, (int)D, cos_t, sin_t, (__nv_bfloat16*)q_out, (__nv_bfloat16*)k_cache, (__nv_bfloat16*)v_cache, (int)Lmax);
+    return launch_pdl(rope_kv_kernel<__nv_bfloat16>, dim3(M), dim3(256), 0, st, (const __nv_bfloat16*)q, ldq, (const __nv_bfloat16*)k, ldk, (const __nv_bfloat16*)v, ldv, pos0, (int)S, (int)Hq, (int)Hkv, (int)D, cos_t, sin_t, (__nv_bfloat16*)q_out, (__nv_bfloat16*)k_cache, (__nv_bfloat16*)v_cache, (int)Lmax);
   else
-    rope_kv_kernel<__half><<<M, 256, 0, st>>>((const __half*)q, ldq, (const __half*)k, ldk, (const __half*)v, ldv, pos0, (int)S, (int)Hq, (int)Hkv, (int)D, cos_t, sin_t, (__half*)q_out, (__half*)k_cache, (__half*)v_cache, (int)Lmax);
-  return launch_status();
+    return launch_pdl(rope_kv_kernel<__half>, dim3(M), dim3(256), 0, st, (const __half*)q, ldq, (const __half*)k, ldk, (const __half*)v, ldv, pos0, (int)S, (int)Hq, (int)Hkv, (int)D, cos_t, sin_t, (__half*)q_out, (__half*)k_cache, (__half*)v_cache, (int)Lmax);
 }
 
 extern "C" int64_t csaq_attention_workspace_floats(int64_t B, int64_t S, int64_t Hq, int64_t Hkv,
@@ -295,10 +305,9 @@ extern "C" int csaq_decode_attention(const void* q, const void* k_cache, const v
   const dim3 grid((unsigned)(B * Hkv), (unsigned)((Lmax + kChunk - 1) / kChunk));
   cudaStream_t st = as_stream(stream);
   if (dtype == CSAQ_DT_BF16)
-    attention_kernel<__nv_bfloat16><<<grid, kAttnWarps * 32, 0, st>>>((const __nv_bfloat16*)q, (const __nv_bfloat16*)k_cache, (const __nv_bfloat16*)v_cache, pos0, (int)S, (int)Hq, (int)Hkv, (int)Lmax, scale, part, tickets, (__nv_bfloat16*)out);
+    return launch_pdl(attention_kernel<__nv_bfloat16>, dim3(grid), dim3(kAttnWarps * 32), 0, st, (const __nv_bfloat16*)q, (const __nv_bfloat16*)k_cache, (const __nv_bfloat16*)v_cache, pos0, (int)S, (int)Hq, (int)Hkv, (int)Lmax, scale, part, tickets, (__nv_bfloat16*)out);
   else
-    attention_kernel<__half><<<grid, kAttnWarps * 32, 0, st>>>((const __half*)q, (const __half*)k_cache, (const __half*)v_cache, pos0, (int)S, (int)Hq, (int)Hkv, (int)Lmax, scale, part, tickets, (__half*)out);
-  return launch_status();
+    return launch_pdl(attention_kernel<__half>, dim3(grid), dim3(kAttnWarps * 32), 0, st, (const __half*)q, (const __half*)k_cache, (const __half*)v_cache, pos0, (int)S, (int)Hq, (int)Hkv, (int)Lmax, scale, part, tickets, (__half*)out);
 }
 
 extern "C" int csaq_silu_mul(const void* g, int64_t ldg, const void* u, int64_t ldu, void* h,
@@ -308,10 +317,9 @@ extern "C" int csaq_silu_mul(const void* g, int64_t ldg, const void* u, int64_t 
   if (M == 0) return CSAQ_OK;
   cudaStream_t st = as_stream(stream);
   if (dtype == CSAQ_DT_BF16)
-    silu_mul_kernel<__nv_bfloat16><<<blocks_for(M * N), 256, 0, st>>>((const __nv_bfloat16*)g, ldg, (const __nv_bfloat16*)u, ldu, (__nv_bfloat16*)h, ldh, M, (int)N);
+    return launch_pdl(silu_mul_kernel<__nv_bfloat16>, dim3(blocks_for(M * N)), dim3(256), 0, st, (const __nv_bfloat16*)g, ldg, (const __nv_bfloat16*)u, ldu, (__nv_bfloat16*)h, ldh, M, (int)N);
   else
-    silu_mul_kernel<__half><<<blocks_for(M * N), 256, 0, st>>>((const __half*)g, ldg, (const __half*)u, ldu, (__half*)h, ldh, M, (int)N);
-  return launch_status();
+    return launch_pdl(silu_mul_kernel<__half>, dim3(blocks_for(M * N)), dim3(256), 0, st, (const __half*)g, ldg, (const __half*)u, ldu, (__half*)h, ldh, M, (int)N);
 }
 
 extern "C" int csaq_spec_accept(const int64_t* draft, const int64_t* verify_argmax, int64_t B,
@@ -321,10 +329,9 @@ extern "C" int csaq_spec_accept(const int64_t* draft, const int64_t* verify_argm
   if (!draft || !verify_argmax || !pos0 || !out_tokens || !n_out || !next_tok || !n_new || !stats || !remaining)
     return CSAQ_ERR_ARG;
   if (B <= 0 || K <= 0 || cap <= 0) return CSAQ_ERR_ARG;
-  accept_kernel<<<blocks_for(B, 128), 128, 0, as_stream(stream)>>>(draft, verify_argmax, (int)B, (int)K,
-                                                                  pos0, out_tokens, n_out, (int)cap,
-                                                                  next_tok, n_new, stats, remaining);
-  return launch_status();
+  return launch_pdl(accept_kernel, dim3(blocks_for(B, 128)), dim3(128), 0, as_stream(stream), draft,
+                    verify_argmax, (int)B, (int)K, pos0, out_tokens, n_out, (int)cap, next_tok, n_new, stats,
+                    remaining);
 }
 
 extern "C" int csaq_greedy_commit(const int64_t* tok, int64_t B, int32_t* pos0, int64_t* out_tokens,
@@ -332,9 +339,8 @@ extern "C" int csaq_greedy_commit(const int64_t* tok, int64_t B, int32_t* pos0, 
                                   void* stream) {
   if (!tok || !pos0 || !out_tokens || !n_out || !next_tok || !remaining || B <= 0 || cap <= 0)
     return CSAQ_ERR_ARG;
-  commit_kernel<<<blocks_for(B, 128), 128, 0, as_stream(stream)>>>(tok, (int)B, pos0, out_tokens, n_out,
-                                                                  (int)cap, next_tok, remaining);
-  return launch_status();
+  return launch_pdl(commit_kernel, dim3(blocks_for(B, 128)), dim3(128), 0, as_stream(stream), tok, (int)B,
+                    pos0, out_tokens, n_out, (int)cap, next_tok, remaining);
 }
 
 // ── csaq_decode_attention_static: decode attention with library-owned scratch
