@@ -20,34 +20,90 @@ __device__ __forceinline__ float round_to(float v) {
 }
 
 // ── RMSNorm (HF Llama/Qwen2): y = w * T(x * rsqrt(mean(x^2) + eps)) ─────────
+// One CTA per row. Rows whose length is a multiple of 8 (16-byte aligned)
+// take a vector path: every thread loads its x and w vectors up front (one
+// memory round trip), keeps x in registers and writes 16-byte stores.
+constexpr int kNormThreads = 256;
+constexpr int kNormVec = 4;  // 16-byte vectors per thread kept in registers (H <= 8192)
+
 template <typename T>
-__global__ void rmsnorm_kernel(const T* __restrict__ x, int64_t ldx, const T* __restrict__ w,
-                               T* __restrict__ y, int64_t ldy, int H, float eps) {
+__device__ __forceinline__ float block_sum(float v, float* red) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    float t = threadIdx.x < (blockDim.x >> 5) ? red[threadIdx.x] : 0.0f;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) t += __shfl_xor_sync(0xffffffffu, t, o);
+    if (threadIdx.x == 0) red[0] = t;
+  }
+  __syncthreads();
+  return red[0];
+}
+
+template <typename T>
+__global__ void __launch_bounds__(kNormThreads) rmsnorm_kernel(const T* __restrict__ x, int64_t ldx,
+                                                               const T* __restrict__ w, T* __restrict__ y,
+                                                               int64_t ldy, int H, float eps) {
   pdl_wait();
   pdl_trigger();
   const int64_t row = blockIdx.x;
   const T* xr = x + row * ldx;
+  T* yr = y + row * ldy;
   __shared__ float red[32];
+  const bool vec = (H % 8 == 0) && H <= kNormThreads * 8 * kNormVec &&
+                   (reinterpret_cast<uintptr_t>(xr) % 16 == 0) && (reinterpret_cast<uintptr_t>(yr) % 16 == 0) &&
+                   (reinterpret_cast<uintptr_t>(w) % 16 == 0);
+  if (vec) {
+    const int nv = H / 8;
+    uint4 xv[kNormVec], wv[kNormVec];
+    float ss = 0.0f;
+#pragma unroll
+    for (int j = 0; j < kNormVec; ++j) {
+      const int i = threadIdx.x + j * kNormThreads;
+      if (i < nv) {
+        xv[j] = reinterpret_cast<const uint4*>(xr)[i];
+        wv[j] = reinterpret_cast<const uint4*>(w)[i];
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < kNormVec; ++j) {
+      const int i = threadIdx.x + j * kNormThreads;
+      if (i < nv) {
+        const T* e = reinterpret_cast<const T*>(&xv[j]);
+#pragma unroll
+        for (int t = 0; t < 8; ++t) {
+          const float v = to_f32<T>(e[t]);
+          ss = fmaf(v, v, ss);
+        }
+      }
+    }
+    const float r = rsqrtf(block_sum<T>(ss, red) / (float)H + eps);
+#pragma unroll
+    for (int j = 0; j < kNormVec; ++j) {
+      const int i = threadIdx.x + j * kNormThreads;
+      if (i < nv) {
+        const T* e = reinterpret_cast<const T*>(&xv[j]);
+        const T* we = reinterpret_cast<const T*>(&wv[j]);
+        uint4 o;
+        T* oe = reinterpret_cast<T*>(&o);
+#pragma unroll
+        for (int t = 0; t < 8; ++t) oe[t] = from_f32<T>(to_f32<T>(we[t]) * round_to<T>(to_f32<T>(e[t]) * r));
+        reinterpret_cast<uint4*>(yr)[i] = o;
+      }
+    }
+    return;
+  }
   float ss = 0.0f;
   for (int i = threadIdx.x; i < H; i += blockDim.x) {
     const float v = to_f32<T>(xr[i]);
     ss = fmaf(v, v, ss);
   }
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
-  __syncthreads();
-  if (threadIdx.x < 32) {
-    float v = threadIdx.x < (blockDim.x >> 5) ? red[threadIdx.x] : 0.0f;
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-    if (threadIdx.x == 0) red[0] = v;
-  }
-  __syncthreads();
-  const float r = rsqrtf(red[0] / (float)H + eps);
+  const float r = rsqrtf(block_sum<T>(ss, red) / (float)H + eps);
   for (int i = threadIdx.x; i < H; i += blockDim.x) {
     const float n = round_to<T>(to_f32<T>(xr[i]) * r);
-    y[row * ldy + i] = from_f32<T>(to_f32<T>(w[i]) * n);
+    yr[i] = from_f32<T>(to_f32<T>(w[i]) * n);
   }
 }
 
@@ -56,6 +112,11 @@ __global__ void rmsnorm_kernel(const T* __restrict__ x, int64_t ldx, const T* __
 // cos/sin: (Lmax, D) fp32 holding the model-dtype-rounded values.
 // rotate_half convention: out_i = x_i cos_i - x_{i+D/2} sin_i (i < D/2),
 //                         out_i = x_i cos_i + x_{i-D/2} sin_i (i >= D/2).
+// One thread per (token, head, 8 rotary pairs): it loads x[i..i+8) and
+// x[i+D/2..i+D/2+8) of its head (16-byte vectors) and the matching cos/sin,
+// so every rotation is local and all loads go out in one round trip. Heads
+// Hq .. Hq+Hkv-1 are the key heads (rotated into the cache); the value
+// heads are copied to the cache by threads of their own.
 template <typename T>
 __global__ void rope_kv_kernel(const T* __restrict__ q, int64_t ldq, const T* __restrict__ k,
                                int64_t ldk, const T* __restrict__ v, int64_t ldv,
@@ -65,28 +126,62 @@ __global__ void rope_kv_kernel(const T* __restrict__ q, int64_t ldq, const T* __
                                T* __restrict__ v_cache, int Lmax) {
   pdl_wait();
   pdl_trigger();
-  const int64_t m = blockIdx.x;  // token
+  const int64_t m = blockIdx.y;  // token
   const int b = (int)(m / S), s = (int)(m % S);
   const int pos = pos0[b] + s;
-  const float* cs = cos_t + (int64_t)pos * D;
-  const float* sn = sin_t + (int64_t)pos * D;
-  const int half = D / 2;
-  for (int idx = threadIdx.x; idx < (Hq + Hkv) * D; idx += blockDim.x) {
-    const int hh = idx / D, i = idx % D;
+  const int half = D / 2, gpr = half / 8;  // 8-pair groups per head
+  const int rot = (Hq + Hkv) * gpr;          // rotation work items of the token
+  const int cpy = Hkv * (D / 8);             // value vectors of the token
+  const int idx = blockIdx.x * blockDim.x + threadIdx.x;
+  if (idx < rot) {
+    const int hh = idx / gpr, i0 = (idx % gpr) * 8;
     const bool is_q = hh < Hq;
     const int h = is_q ? hh : hh - Hq;
     const T* src = is_q ? q + m * ldq + (int64_t)h * D : k + m * ldk + (int64_t)h * D;
-    const float xi = to_f32<T>(src[i]);
-    const float xo = to_f32<T>(src[i < half ? i + half : i - half]);
-    const float r = i < half ? fmaf(xi, cs[i], -xo * sn[i]) : fmaf(xi, cs[i], xo * sn[i]);
-    if (is_q) {
-      q_out[(m * Hq + h) * D + i] = from_f32<T>(r);
-    } else {
-      const int64_t c = (((int64_t)b * Hkv + h) * Lmax + pos) * D + i;
-      k_cache[c] = from_f32<T>(r);
-      v_cache[c] = v[m * ldv + (int64_t)h * D + i];
+    const uint4 a = *reinterpret_cast<const uint4*>(src + i0);
+    const uint4 c = *reinterpret_cast<const uint4*>(src + i0 + half);
+    const float* cs = cos_t + (int64_t)pos * D;
+    const float* sn = sin_t + (int64_t)pos * D;
+    float ca[8], sa[8], cb[8], sb[8];
+#pragma unroll
+    for (int t = 0; t < 2; ++t) {
+      const float4 c0 = reinterpret_cast<const float4*>(cs + i0)[t];
+      const float4 s0 = reinterpret_cast<const float4*>(sn + i0)[t];
+      const float4 c1 = reinterpret_cast<const float4*>(cs + i0 + half)[t];
+      const float4 s1 = reinterpret_cast<const float4*>(sn + i0 + half)[t];
+      ca[4 * t] = c0.x; ca[4 * t + 1] = c0.y; ca[4 * t + 2] = c0.z; ca[4 * t + 3] = c0.w;
+      sa[4 * t] = s0.x; sa[4 * t + 1] = s0.y; sa[4 * t + 2] = s0.z; sa[4 * t + 3] = s0.w;
+      cb[4 * t] = c1.x; cb[4 * t + 1] = c1.y; cb[4 * t + 2] = c1.z; cb[4 * t + 3] = c1.w;
+      sb[4 * t] = s1.x; sb[4 * t + 1] = s1.y; sb[4 * t + 2] = s1.z; sb[4 * t + 3] = s1.w;
     }
+    const T* ae = reinterpret_cast<const T*>(&a);
+    const T* ce = reinterpret_cast<const T*>(&c);
+    uint4 lo, hi;
+    T* le = reinterpret_cast<T*>(&lo);
+    T* he = reinterpret_cast<T*>(&hi);
+#pragma unroll
+    for (int t = 0; t < 8; ++t) {
+      const float x0 = to_f32<T>(ae[t]), x1 = to_f32<T>(ce[t]);
+      le[t] = from_f32<T>(fmaf(x0, ca[t], -x1 * sa[t]));
+      he[t] = from_f32<T>(fmaf(x1, cb[t], x0 * sb[t]));
+    }
+    T* dst = is_q ? q_out + (m * Hq + h) * D : k_cache + (((int64_t)b * Hkv + h) * Lmax + pos) * D;
+    *reinterpret_cast<uint4*>(dst + i0) = lo;
+    *reinterpret_cast<uint4*>(dst + i0 + half) = hi;
+  } else if (idx < rot + cpy) {
+    const int j = idx - rot, h = j / (D / 8), i0 = (j % (D / 8)) * 8;
+    *reinterpret_cast<uint4*>(v_cache + (((int64_t)b * Hkv + h) * Lmax + pos) * D + i0) =
+        *reinterpret_cast<const uint4*>(v + m * ldv + (int64_t)h * D + i0);
   }
+}
+
+// 16-byte asynchronous global -> shared copies
+__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(static_cast<uint32_t>(__cvta_generic_to_shared(dst))),
+               "l"(src));
+}
+__device__ __forceinline__ void cp_async_commit_wait_all() {
+  asm volatile("cp.async.commit_group;\n\tcp.async.wait_group 0;" ::: "memory");
 }
 
 // ── decode attention (GQA, causal over the new tokens) ──────────────────────
@@ -117,10 +212,12 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attention_kernel(
   const int n_keys = max(0, min(kChunk, len - k0));
   const T* kb = k_cache + (((int64_t)b * Hkv + h) * Lmax + k0) * D;
   const T* vb = v_cache + (((int64_t)b * Hkv + h) * Lmax + k0) * D;
+  // the chunk's keys and values: one wave of 16-byte asynchronous copies
   for (int e = threadIdx.x; e < n_keys * D / 8; e += blockDim.x) {
-    reinterpret_cast<uint4*>(&ks[0][0])[e] = reinterpret_cast<const uint4*>(kb)[e];
-    reinterpret_cast<uint4*>(&vs[0][0])[e] = reinterpret_cast<const uint4*>(vb)[e];
+    cp_async16(reinterpret_cast<uint4*>(&ks[0][0]) + e, reinterpret_cast<const uint4*>(kb) + e);
+    cp_async16(reinterpret_cast<uint4*>(&vs[0][0]) + e, reinterpret_cast<const uint4*>(vb) + e);
   }
+  cp_async_commit_wait_all();
   __syncthreads();
   // partial layout: [bh][sp][r][D + 2]
   float* pbase = part + ((int64_t)bh * n_split + sp) * R * (D + 2);
@@ -133,7 +230,35 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attention_kernel(
     for (int i = 0; i < 4; ++i) qv[i] = to_f32<T>(qr[lane * 4 + i]) * scale;
     const int kmax = min(n_keys, qpos - k0 + 1);
     float m = -INFINITY, l = 0.0f, o[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-    for (int j = 0; j < kmax; ++j) {
+    int j = 0;
+    for (; j + 4 <= kmax; j += 4) {  // four keys per step: independent dot products
+      float d[4];
+#pragma unroll
+      for (int t = 0; t < 4; ++t) {
+        d[t] = 0.0f;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) d[t] = fmaf(qv[i], to_f32<T>(ks[j + t][lane * 4 + i]), d[t]);
+      }
+#pragma unroll
+      for (int off = 16; off > 0; off >>= 1)
+#pragma unroll
+        for (int t = 0; t < 4; ++t) d[t] += __shfl_xor_sync(0xffffffffu, d[t], off);
+      const float mn = fmaxf(fmaxf(m, fmaxf(d[0], d[1])), fmaxf(d[2], d[3]));
+      const float corr = __expf(m - mn);
+      float p[4];
+#pragma unroll
+      for (int t = 0; t < 4; ++t) p[t] = __expf(d[t] - mn);
+      l = fmaf(l, corr, (p[0] + p[1]) + (p[2] + p[3]));
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        float acc = o[i] * corr;
+#pragma unroll
+        for (int t = 0; t < 4; ++t) acc = fmaf(p[t], to_f32<T>(vs[j + t][lane * 4 + i]), acc);
+        o[i] = acc;
+      }
+      m = mn;
+    }
+    for (; j < kmax; ++j) {
       float d = 0.0f;
 #pragma unroll
       for (int i = 0; i < 4; ++i) d = fmaf(qv[i], to_f32<T>(ks[j][lane * 4 + i]), d);
@@ -161,9 +286,11 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attention_kernel(
   for (int r = warp; r < R; r += kAttnWarps) {
     const int s = r / G, hq = h * G + r % G;
     float M_ = -INFINITY;
+#pragma unroll 8
     for (int p = 0; p < n_split; ++p)
       M_ = fmaxf(M_, __ldcg(part + (((int64_t)bh * n_split + p) * R + r) * (D + 2) + D));
     float L = 0.0f, o[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+#pragma unroll 4
     for (int p = 0; p < n_split; ++p) {
       const float* pr = part + (((int64_t)bh * n_split + p) * R + r) * (D + 2);
       const float mp = __ldcg(pr + D);
@@ -266,9 +393,9 @@ extern "C" int csaq_rmsnorm(const void* x, int64_t ldx, const void* w, void* y, 
   if (M == 0) return CSAQ_OK;
   cudaStream_t st = as_stream(stream);
   if (dtype == CSAQ_DT_BF16)
-    return launch_pdl(rmsnorm_kernel<__nv_bfloat16>, dim3(M), dim3(256), 0, st, (const __nv_bfloat16*)x, ldx, (const __nv_bfloat16*)w, (__nv_bfloat16*)y, ldy, (int)H, eps);
+    return launch_pdl(rmsnorm_kernel<__nv_bfloat16>, dim3(M), dim3(kNormThreads), 0, st, (const __nv_bfloat16*)x, ldx, (const __nv_bfloat16*)w, (__nv_bfloat16*)y, ldy, (int)H, eps);
   else
-    return launch_pdl(rmsnorm_kernel<__half>, dim3(M), dim3(256), 0, st, (const __half*)x, ldx, (const __half*)w, (__half*)y, ldy, (int)H, eps);
+    return launch_pdl(rmsnorm_kernel<__half>, dim3(M), dim3(kNormThreads), 0, st, (const __half*)x, ldx, (const __half*)w, (__half*)y, ldy, (int)H, eps);
 }
 
 extern "C" int csaq_rope_kv(const void* q, int64_t ldq, const void* k, int64_t ldk, const void* v,
@@ -279,12 +406,23 @@ extern "C" int csaq_rope_kv(const void* q, int64_t ldq, const void* k, int64_t l
   if (!q || !k || !v || !pos0 || !cos_t || !sin_t || !q_out || !k_cache || !v_cache) return CSAQ_ERR_ARG;
   if (B <= 0 || S <= 0 || Hq <= 0 || Hkv <= 0 || D <= 0 || D % 2 || Lmax <= 0) return CSAQ_ERR_ARG;
   if (dtype != CSAQ_DT_F16 && dtype != CSAQ_DT_BF16) return CSAQ_ERR_ARG;
+  // 16-byte vectors of 8 rotary pairs: D % 16 == 0, rows 16-byte aligned
+  auto a16 = [](const void* p) { return reinterpret_cast<uintptr_t>(p) % 16 == 0; };
+  if (D % 16 || ldq % 8 || ldk % 8 || ldv % 8 || !a16(q) || !a16(k) || !a16(v) || !a16(q_out) ||
+      !a16(k_cache) || !a16(v_cache) || !a16(cos_t) || !a16(sin_t))
+    return CSAQ_ERR_UNSUPPORTED;
   cudaStream_t st = as_stream(stream);
   const int64_t M = B * S;
+  const int64_t work = (Hq + Hkv) * (D / 16) + Hkv * (D / 8);
+  const dim3 grid((unsigned)((work + 255) / 256), (unsigned)M);
   if (dtype == CSAQ_DT_BF16)
-    return launch_pdl(rope_kv_kernel<__nv_bfloat16>, dim3(M), dim3(256), 0, st, (const __nv_bfloat16*)q, ldq, (const __nv_bfloat16*)k, ldk, (const __nv_bfloat16*)v, ldv, pos0, (int)S, (int)Hq, (int)Hkv, (int)D, cos_t, sin_t, (__nv_bfloat16*)q_out, (__nv_bfloat16*)k_cache, (__nv_bfloat16*)v_cache, (int)Lmax);
-  else
-    return launch_pdl(rope_kv_kernel<__half>, dim3(M), dim3(256), 0, st, (const __half*)q, ldq, (const __half*)k, ldk, (const __half*)v, ldv, pos0, (int)S, (int)Hq, (int)Hkv, (int)D, cos_t, sin_t, (__half*)q_out, (__half*)k_cache, (__half*)v_cache, (int)Lmax);
+    return launch_pdl(rope_kv_kernel<__nv_bfloat16>, grid, dim3(256), 0, st, (const __nv_bfloat16*)q, ldq,
+                      (const __nv_bfloat16*)k, ldk, (const __nv_bfloat16*)v, ldv, pos0, (int)S, (int)Hq, (int)Hkv,
+                      (int)D, cos_t, sin_t, (__nv_bfloat16*)q_out, (__nv_bfloat16*)k_cache,
+                      (__nv_bfloat16*)v_cache, (int)Lmax);
+  return launch_pdl(rope_kv_kernel<__half>, grid, dim3(256), 0, st, (const __half*)q, ldq, (const __half*)k, ldk,
+                    (const __half*)v, ldv, pos0, (int)S, (int)Hq, (int)Hkv, (int)D, cos_t, sin_t,
+                    (__half*)q_out, (__half*)k_cache, (__half*)v_cache, (int)Lmax);
 }
 
 extern "C" int64_t csaq_attention_workspace_floats(int64_t B, int64_t S, int64_t Hq, int64_t Hkv,
