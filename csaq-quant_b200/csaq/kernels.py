@@ -497,6 +497,30 @@ class CSAQLinear(nn.Module):
         del linear.weight
         return layer
 
+    @classmethod
+    def empty_tiers(cls, in_features: int, out_features: int, tiers: Dict[int, int], group_size: int = 128,
+                    bias: Optional[torch.Tensor] = None) -> "CSAQLinear":
+        """A mixed-row layer with zeroed tier buffers of the given row counts,
+        to be filled by load_state_dict (the loader of exported models)."""
+        dominant = max(tiers, key=tiers.__getitem__)
+        layer = cls(in_features=in_features, out_features=out_features, bits=dominant, bias=bias,
+                    group_size=group_size)
+        layer.weight_packed = torch.zeros(0, dtype=torch.uint8)
+        layer.weight_scales = torch.zeros(0, dtype=torch.float32)
+        layer.weight_zp = torch.zeros(0, dtype=torch.int32)
+        G = (in_features + group_size - 1) // group_size if group_size > 0 else 1
+        for b in sorted(tiers, reverse=True):
+            n = int(tiers[b])
+            if b != 16:
+                _assert_supported(b)
+            g = 1 if b == 16 else G
+            layer.register_buffer(f"tier{b}_rows", torch.zeros(n, dtype=torch.int32))
+            layer.register_buffer(f"tier{b}_packed", torch.zeros(n, _packed_cols(in_features, b), dtype=torch.uint8))
+            layer.register_buffer(f"tier{b}_scales", torch.ones(n, g, dtype=torch.float32))
+            layer.register_buffer(f"tier{b}_zp", torch.zeros(n, g, dtype=torch.int32))
+            layer.tier_bits.append(b)
+        return layer
+
     # ── verify-pass protection (apply_csaq, csaq/core.py:393-407) ───────────
     def set_protected_rows(self, hi_rows: torch.Tensor, fp16_backup: torch.Tensor) -> None:
         """Register the protected rows and their fp16 weights.
