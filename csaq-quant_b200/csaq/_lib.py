@@ -84,6 +84,8 @@ _SIGNATURES = {
                                       ctypes.c_float, c_vp, c_vp, c_vp, c_int, c_vp]),
     "csaq_decode_attention_static": (c_int, [c_vp, c_vp, c_vp, c_vp, c_i64, c_i64, c_i64, c_i64, c_i64, c_i64,
                                              ctypes.c_float, c_vp, c_int, c_vp]),
+    "csaq_rank_sum": (c_int, [c_vp, c_int, c_i64, c_i64, c_vp, c_i64, c_i64, c_i64, c_int, c_int, c_vp]),
+    "csaq_argmax_parts": (c_int, [c_vp, c_int, c_i64, c_i64, c_i64, c_i64, c_vp, c_int, c_vp]),
     "csaq_silu_mul": (c_int, [c_vp, c_i64, c_vp, c_i64, c_vp, c_i64, c_i64, c_i64, c_int, c_vp]),
     "csaq_spec_accept": (c_int, [c_vp, c_vp, c_i64, c_i64, c_vp, c_vp, c_vp, c_i64, c_vp, c_vp, c_vp, c_vp, c_vp]),
     "csaq_greedy_commit": (c_int, [c_vp, c_i64, c_vp, c_vp, c_vp, c_i64, c_vp, c_vp, c_vp]),

@@ -113,8 +113,9 @@ class CSAQInferenceEngine:
     """Self-speculative decoding engine (csaq/inference.py:125-574)."""
 
     def __init__(self, model: nn.Module, causal_map: Dict[str, List[int]], tokenizer: Optional[Any] = None,
-                 verbose: bool = True) -> None:
+                 verbose: bool = True, tp_group: Any = None) -> None:
         self.model = model
+        self.tp_group = tp_group  # torch.distributed group: tensor-parallel decode runtime
         self.causal_map = causal_map
         self.tokenizer = tokenizer
         self.verbose = verbose
@@ -244,7 +245,8 @@ class CSAQInferenceEngine:
             torch.cuda.empty_cache()
             L = max(max_len, 64)
             L = (L + 63) // 64 * 64
-            rt = DecodeRuntime(self.model, max_batch=batch, max_len=L, lookahead=lookahead)
+            rt = DecodeRuntime(self.model, max_batch=batch, max_len=L, lookahead=lookahead,
+                               tp_group=self.tp_group)
             self._runtime, self._runtime_key = rt, key
         return rt
 

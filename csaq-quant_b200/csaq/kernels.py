@@ -521,6 +521,85 @@ class CSAQLinear(nn.Module):
             layer.tier_bits.append(b)
         return layer
 
+    # ── tensor-parallel shards ──────────────────────────────────────────────
+    def tp_shard(self, dim: str, rank: int, world: int) -> "CSAQLinear":
+        """The rank's part of this layer for tensor parallelism, as a mixed-row
+        layer. ``dim="col"``: output rows [rank*N/world, (rank+1)*N/world);
+        ``dim="row"``: input columns [rank*K/world, ...), which must be a
+        multiple of 128 wide so quantisation groups stay whole (the bias then
+        stays on rank 0 only, because the partial outputs are summed).
+        Protected rows and their fp16 copies are split the same way."""
+        N, K = self.out_features, self.in_features
+        if dim not in ("col", "row"):
+            raise ValueError("dim must be 'col' or 'row'")
+        full = N if dim == "col" else K
+        if full % world:
+            raise ValueError(f"{full} does not split over {world} ranks")
+        lo, hi = rank * full // world, (rank + 1) * full // world
+        if dim == "row" and (lo % 128 or hi % 128):
+            raise ValueError("row shards must be 128-column aligned")
+        hi_rows = getattr(self, "_csaq_hi_rows", None)
+        bk = getattr(self, "_csaq_fp16_backup", None)
+        bias = self.bias
+        # the tiers as stored (on the buffers' own device), protected rows last in each
+        src = []
+        if self.tier_bits:
+            for b in self.tier_bits:
+                sc = getattr(self, f"tier{b}_scales")
+                src.append((b, getattr(self, f"tier{b}_rows").long(), getattr(self, f"tier{b}_packed"),
+                            sc.reshape(sc.shape[0], -1), getattr(self, f"tier{b}_zp").reshape(sc.shape[0], -1)))
+        else:
+            b = self.bits
+            rows = torch.arange(N, device=self.weight_packed.device)
+            codes = self.weight_packed.reshape(N, -1)
+            sc, zp = self.weight_scales.reshape(N, -1).float(), self.weight_zp.reshape(N, -1)
+            if hi_rows is not None and hi_rows.numel():
+                prot = torch.zeros(N, dtype=torch.bool, device=rows.device)
+                prot[hi_rows.to(rows.device)] = True
+                order = torch.cat([rows[~prot], rows[prot]])
+                rows, codes, sc, zp = order, codes[order], sc[order], zp[order]
+            src.append((b, rows, codes, sc, zp))
+        parts = []
+        for b, rows, codes, sc, zp in src:
+            if dim == "col":
+                keep = (rows >= lo) & (rows < hi)
+                rows, codes, sc, zp = rows[keep] - lo, codes[keep], sc[keep], zp[keep]
+            else:
+                b0, b1 = (lo * b) // 8, (hi * b) // 8
+                codes = codes[:, b0:b1]
+                if b != 16 and sc.shape[-1] > 1:
+                    gs = K // sc.shape[-1] if self.group_size <= 0 else self.group_size
+                    g0, g1 = lo // gs, hi // gs
+                    sc, zp = sc[:, g0:g1], zp[:, g0:g1]
+            if rows.numel():
+                parts.append((b, rows, codes, sc, zp.to(torch.int32)))
+        n_out, n_in = (hi - lo, K) if dim == "col" else (N, hi - lo)
+        if dim == "col":
+            b_sh = None if bias is None else bias[lo:hi]
+        else:
+            b_sh = bias if rank == 0 else None
+        grouped = self.tier_bits and 0 < self.group_size < K or (not self.tier_bits and self.weight_scales.dim() == 2)
+        counts = {b: r.numel() for b, r, *_ in parts}
+        out = CSAQLinear(n_in, n_out, max(counts, key=counts.__getitem__), bias=b_sh,
+                         group_size=self.group_size if grouped else -1)
+        dev = parts[0][2].device
+        out.weight_packed = torch.zeros(0, dtype=torch.uint8, device=dev)
+        out.weight_scales = torch.zeros(0, dtype=torch.float32, device=dev)
+        out.weight_zp = torch.zeros(0, dtype=torch.int32, device=dev)
+        for b, rows, codes, sc, zp in parts:
+            out.register_buffer(f"tier{b}_rows", rows.to(torch.int32).contiguous())
+            out.register_buffer(f"tier{b}_packed", codes.contiguous())
+            out.register_buffer(f"tier{b}_scales", sc.reshape(rows.numel(), -1).contiguous())
+            out.register_buffer(f"tier{b}_zp", zp.reshape(rows.numel(), -1).contiguous())
+            out.tier_bits.append(b)
+        if hi_rows is not None and hi_rows.numel():
+            if dim == "col":
+                keep = (hi_rows >= lo) & (hi_rows < hi)
+                out.set_protected_rows(hi_rows[keep] - lo, bk[keep])
+            else:
+                out.set_protected_rows(hi_rows, bk[:, lo:hi])
+        return out
+
     # ── verify-pass protection (apply_csaq, csaq/core.py:393-407) ───────────
     def set_protected_rows(self, hi_rows: torch.Tensor, fp16_backup: torch.Tensor) -> None:
         """Register the protected rows and their fp16 weights.

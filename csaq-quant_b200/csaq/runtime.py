@@ -11,8 +11,15 @@ the on-device acceptance) is captured once as a CUDA graph and replayed:
 
 The unquantised lm_head runs as an fp16 tier of the same GEMV kernel (every
 token's logits are independent of the launch's token count, so speculative
-and one-token decoding agree exactly); the embedding gather and the
-vocabulary argmax use torch (ATen) kernels.
+and one-token decoding agree exactly); the embedding gather uses torch.
+
+Tensor parallel (tp_group of W ranks): each rank holds column shards of
+q/k/v/gate/up (its heads and its slice of the MLP width), row shards of
+o/down (the matching input slice) and a vocabulary slice of the lm_head.
+After o and down every rank all-gathers the partial outputs and adds them to
+the residual stream in rank order (csaq_rank_sum), so a token's result does
+not depend on how many tokens share the step; the greedy token is the argmax
+over the gathered vocabulary slices.
 
 Weights: the draft pass reads only the quantised tiers; the verify pass
 reads the tiers without their protected rows plus the fp16 copies of those
@@ -72,15 +79,22 @@ class _Shape:
     logits: torch.Tensor
     part: torch.Tensor
     descs: Dict  # (layer, name, verify) -> ctypes array + count
+    y_part: Optional[torch.Tensor] = None    # TP: this rank's partial o/down output (M, H)
+    y_all: Optional[torch.Tensor] = None     # TP: all ranks' partials (W, M, H)
+    logits_all: Optional[torch.Tensor] = None  # TP: all ranks' vocabulary slices (W, M, V/W)
 
 
 class DecodeRuntime:
     """Decode / self-speculative generation for a quantised Llama/Qwen2 model."""
 
     def __init__(self, model: nn.Module, max_batch: int, max_len: int, lookahead: int = 4,
-                 prefill_chunk: int = 64):
+                 prefill_chunk: int = 64, tp_group=None):
         if not supports(model):
             raise ValueError("model is not a Llama/Qwen2 decoder with CSAQLinear layers")
+        import torch.distributed as dist
+        self.tp_group = tp_group
+        self.tp = dist.get_world_size(tp_group) if tp_group is not None else 1
+        self.tp_rank = dist.get_rank(tp_group) if tp_group is not None else 0
         cfg = model.config
         inner, layers = _layers_of(model)
         self.model = model
@@ -107,11 +121,28 @@ class DecodeRuntime:
         # token's logits are computed independently of how many tokens share
         # the launch, so the verify pass over K+1 tokens and one-token steps
         # give identical logits (and identical argmax)
-        head = nn.Linear(self.H, self.V, bias=False, device="meta")
-        head.weight = nn.Parameter(self.lm_w.detach(), requires_grad=False)
-        self.lm_head = CSAQLinear.from_tiers(head, {16: torch.arange(self.V)}, group_size=self.H)
+        W, r = self.tp, self.tp_rank
+        for what, n in (("query heads", self.Hq), ("KV heads", self.Hkv), ("intermediate", self.I),
+                        ("vocabulary", self.V)):
+            if n % W:
+                raise ValueError(f"{what} ({n}) do not split over {W} ranks")
+        self.Vl = self.V // W  # this rank's vocabulary slice (tensor parallel)
+        head = nn.Linear(self.H, self.Vl, bias=False, device="meta")
+        head.weight = nn.Parameter(self.lm_w[r * self.Vl:(r + 1) * self.Vl].detach(), requires_grad=False)
+        self.lm_head = CSAQLinear.from_tiers(head, {16: torch.arange(self.Vl)}, group_size=self.H)
         self.n_layers = len(layers)
-        L, B, Hkv, D = self.n_layers, self.B, self.Hkv, self.D
+        # this rank's linears: the model's own at TP 1; column shards of
+        # q/k/v/gate/up and row shards of o/down otherwise
+        self.lin = []
+        for layer in layers:
+            a, m = layer.self_attn, layer.mlp
+            mods = {"q": a.q_proj, "k": a.k_proj, "v": a.v_proj, "o": a.o_proj, "gate": m.gate_proj,
+                    "up": m.up_proj, "down": m.down_proj}
+            if W > 1:
+                mods = {k: v.tp_shard("row" if k in ("o", "down") else "col", r, W) for k, v in mods.items()}
+            self.lin.append(mods)
+        self.Hq_l, self.Hkv_l, self.I_l = self.Hq // W, self.Hkv // W, self.I // W
+        L, B, Hkv, D = self.n_layers, self.B, self.Hkv_l, self.D
         self.k_cache = torch.zeros(L, B, Hkv, max_len, D, dtype=self.dtype, device=self.dev)
         self.v_cache = torch.zeros(L, B, Hkv, max_len, D, dtype=self.dtype, device=self.dev)
         self.tickets = torch.zeros(L, B * Hkv, dtype=torch.int32, device=self.dev)
@@ -155,25 +186,31 @@ class DecodeRuntime:
         sh = self.shapes.get(S)
         if sh is not None:
             return sh
-        B, H, D, Hq, Hkv, I = self.B, self.H, self.D, self.Hq, self.Hkv, self.I
+        B, H, D, Hq, Hkv, I = self.B, self.H, self.D, self.Hq_l, self.Hkv_l, self.I_l
+        W = self.tp
         M = B * S
         mk = lambda *s: torch.zeros(*s, dtype=self.dtype, device=self.dev)
         nq, nkv = Hq * D, Hkv * D
         part_n = lib().csaq_attention_workspace_floats(B, S, Hq, Hkv, D, self.Lmax)
         sh = _Shape(S=S, M=M, x=mk(M, H), xn=mk(M, H), qkv=mk(M, nq + 2 * nkv), q_rot=mk(M, nq),
-                    attn=mk(M, nq), gu=mk(M, 2 * I), h=mk(M, I), logits=mk(M, self.V),
+                    attn=mk(M, nq), gu=mk(M, 2 * I), h=mk(M, I), logits=mk(M, self.Vl),
                     part=torch.zeros(max(part_n, 1), dtype=torch.float32, device=self.dev),
                     descs={})
-        for li, layer in enumerate(self.layers):
-            a, m = layer.self_attn, layer.mlp
+        if W > 1:
+            sh.y_part, sh.y_all, sh.logits_all = mk(M, H), mk(W, M, H), mk(W, M, self.Vl)
+        # at TP 1 the o/down GEMVs add the residual in their epilogue; with
+        # TP each rank writes its partial and the combine adds them to x
+        res_out = sh.x if W == 1 else sh.y_part
+        res = sh.x if W == 1 else None
+        for li, mods in enumerate(self.lin):
             for verify in (False, True):
-                qkv = (a.q_proj.gemv_descriptors(sh.qkv[:, :nq], verify)
-                       + a.k_proj.gemv_descriptors(sh.qkv[:, nq:nq + nkv], verify)
-                       + a.v_proj.gemv_descriptors(sh.qkv[:, nq + nkv:], verify))
-                o = a.o_proj.gemv_descriptors(sh.x, verify, residual=sh.x)
-                gu = (m.gate_proj.gemv_descriptors(sh.gu[:, :I], verify)
-                      + m.up_proj.gemv_descriptors(sh.gu[:, I:], verify))
-                dn = m.down_proj.gemv_descriptors(sh.x, verify, residual=sh.x)
+                qkv = (mods["q"].gemv_descriptors(sh.qkv[:, :nq], verify)
+                       + mods["k"].gemv_descriptors(sh.qkv[:, nq:nq + nkv], verify)
+                       + mods["v"].gemv_descriptors(sh.qkv[:, nq + nkv:], verify))
+                o = mods["o"].gemv_descriptors(res_out, verify, residual=res)
+                gu = (mods["gate"].gemv_descriptors(sh.gu[:, :I], verify)
+                      + mods["up"].gemv_descriptors(sh.gu[:, I:], verify))
+                dn = mods["down"].gemv_descriptors(res_out, verify, residual=res)
                 for name, d in (("qkv", qkv), ("o", o), ("gu", gu), ("down", dn)):
                     sh.descs[(li, name, verify)] = (_lib.tier_array(d), len(d))
         d = self.lm_head.gemv_descriptors(sh.logits)
@@ -188,21 +225,29 @@ class DecodeRuntime:
         arr, n = arr_n
         check(lib().csaq_qgemv(arr, n, K, x.data_ptr(), self.dt, M, x.stride(0), st), "qgemv")
 
+    def _combine(self, sh: _Shape, M: int, st: int) -> None:
+        """TP: gather every rank's partial o/down output and add them to x in rank order."""
+        import torch.distributed as dist
+        dist.all_gather_into_tensor(sh.y_all[:, :M], sh.y_part[:M], group=self.tp_group)
+        H = self.H
+        check(lib().csaq_rank_sum(sh.y_all.data_ptr(), self.tp, sh.y_all.stride(0), H, sh.x.data_ptr(), H, M, H, 1,
+                                  self.dt, st), "rank_sum")
+
     @torch.no_grad()
     def step(self, S: int, ids: torch.Tensor, pos: torch.Tensor, verify: bool,
              last_only: bool = False) -> torch.Tensor:
         """Run all layers for B*S tokens (ids: B*S int64, pos: per-sequence
-        start positions) and return the logits buffer (M, V) (or (B, V) rows
-        of the last token of each sequence when last_only)."""
+        start positions) and leave the logits of this rank's vocabulary slice
+        in the shape's logits buffer (M rows, or the B rows of the last token
+        of each sequence when last_only); returns the number of logit rows."""
         sh = self._shape(S)
         L = lib()
         st = torch.cuda.current_stream(self.dev).cuda_stream
-        M, H, D, Hq, Hkv, I = sh.M, self.H, self.D, self.Hq, self.Hkv, self.I
+        M, H, D, Hq, Hkv, I = sh.M, self.H, self.D, self.Hq_l, self.Hkv_l, self.I_l
         nq, nkv = Hq * D, Hkv * D
         torch.index_select(self.embed, 0, ids.view(-1), out=sh.x)
         scale = 1.0 / math.sqrt(D)
         for li, layer in enumerate(self.layers):
-            a, m = layer.self_attn, layer.mlp
             check(L.csaq_rmsnorm(sh.x.data_ptr(), H, layer.input_layernorm.weight.data_ptr(),
                                  sh.xn.data_ptr(), H, M, H, self.eps, self.dt, st), "rmsnorm")
             self._gemv(sh.descs[(li, "qkv", verify)], H, sh.xn, M, st)
@@ -218,27 +263,61 @@ class DecodeRuntime:
                                           self.tickets[li].data_ptr(), sh.attn.data_ptr(), self.dt,
                                           st), "attention")
             self._gemv(sh.descs[(li, "o", verify)], nq, sh.attn, M, st)
+            if self.tp > 1:
+                self._combine(sh, M, st)
             check(L.csaq_rmsnorm(sh.x.data_ptr(), H, layer.post_attention_layernorm.weight.data_ptr(),
                                  sh.xn.data_ptr(), H, M, H, self.eps, self.dt, st), "rmsnorm")
             self._gemv(sh.descs[(li, "gu", verify)], H, sh.xn, M, st)
             check(L.csaq_silu_mul(sh.gu.data_ptr(), sh.gu.stride(0), sh.gu[:, I:].data_ptr(),
                                   sh.gu.stride(0), sh.h.data_ptr(), I, M, I, self.dt, st), "silu_mul")
             self._gemv(sh.descs[(li, "down", verify)], I, sh.h, M, st)
+            if self.tp > 1:
+                self._combine(sh, M, st)
         check(L.csaq_rmsnorm(sh.x.data_ptr(), H, self.final_norm.data_ptr(), sh.xn.data_ptr(), H, M, H,
                              self.eps, self.dt, st), "rmsnorm")
         if last_only and S > 1:
             arr, n = sh.descs[("lm", "last")]
             last = sh.xn[S - 1:]  # rows S-1, 2S-1, ...: the last token of each sequence
             check(L.csaq_qgemv(arr, n, H, last.data_ptr(), self.dt, self.B, S * H, st), "lm_head")
-            return sh.logits[: self.B]
+            return self.B
         self._gemv(sh.descs[("lm", "all")], H, sh.xn, M, st)
-        return sh.logits
+        return M
+
+    def argmax(self, S: int, rows: int, out: torch.Tensor) -> None:
+        """Greedy tokens of the first `rows` logit rows of the last step over
+        the whole vocabulary (gathering every rank's slice under TP)."""
+        sh = self.shapes[S]
+        st = torch.cuda.current_stream(self.dev).cuda_stream
+        Vl = self.Vl
+        if self.tp > 1:
+            src = self._gather_logits(sh, rows)
+            n_parts, pstride = self.tp, rows * Vl
+        else:
+            src, n_parts, pstride = sh.logits, 1, 0
+        check(lib().csaq_argmax_parts(src.data_ptr(), n_parts, pstride, Vl, Vl, rows, out.data_ptr(), self.dt, st),
+              "argmax")
+
+    def logits_full(self, S: int, rows: int) -> torch.Tensor:
+        """The full-vocabulary logits of the last step (a copy; gathers under TP)."""
+        sh = self.shapes[S]
+        if self.tp == 1:
+            return sh.logits[:rows].clone()
+        return self._gather_logits(sh, rows).permute(1, 0, 2).reshape(rows, self.V).clone()
+
+    def _gather_logits(self, sh: _Shape, rows: int) -> torch.Tensor:
+        """Every rank's vocabulary slice of the first `rows` logit rows, as a
+        contiguous (W, rows, V/W) view of the shape's gather buffer."""
+        import torch.distributed as dist
+        out = sh.logits_all.view(-1)[: self.tp * rows * self.Vl].view(self.tp, rows, self.Vl)
+        dist.all_gather_into_tensor(out, sh.logits[:rows], group=self.tp_group)
+        return out
 
     def kernels_per_step(self, S: int) -> int:
         """Own (libcsaq) kernel launches in one step of up to 16 tokens per
-        GEMV launch: per layer 2 RMSNorm, 4 GEMV, RoPE, attention, SiLU; plus
-        the final RMSNorm and the lm_head GEMV."""
-        return self.n_layers * 9 + 2
+        GEMV launch: per layer 2 RMSNorm, 4 GEMV, RoPE, attention, SiLU (and
+        2 rank-order combines under TP); plus the final RMSNorm, the lm_head
+        GEMV and the argmax."""
+        return self.n_layers * (9 + (2 if self.tp > 1 else 0)) + 3
 
     # ── generation ──────────────────────────────────────────────────────────
     @torch.no_grad()
@@ -260,12 +339,11 @@ class DecodeRuntime:
             chunk = prompts[:, s0:s0 + C]
             S = chunk.shape[1]
             self.pos0.fill_(s0)
-            logits = self.step(S, chunk.contiguous().view(-1), self.pos0, verify=verify, last_only=True)
-        self.prefill_logits = logits[: self.B].clone()
-        first = torch.argmax(logits[: self.B], dim=-1)
-        self.out_tokens[:, 0] = first
+            self.step(S, chunk.contiguous().view(-1), self.pos0, verify=verify, last_only=True)
+        self.prefill_logits = self.logits_full(S, self.B)
+        self.argmax(S, self.B, self.next_tok)
+        self.out_tokens[:, 0] = self.next_tok
         self.n_out.fill_(1)
-        self.next_tok.copy_(first)
         self.pos0.fill_(P)
         self.remaining.fill_(max_new - 1)
 
@@ -277,13 +355,13 @@ class DecodeRuntime:
         self.vin[:, 0].copy_(self.next_tok)
         self.cur_pos.copy_(self.pos0)
         for k in range(K):
-            logits = self.step(1, self.next_tok, self.cur_pos, verify=False)
-            torch.argmax(logits[:B], dim=-1, out=self.next_tok)
+            self.step(1, self.next_tok, self.cur_pos, verify=False)
+            self.argmax(1, B, self.next_tok)
             self.draft[:, k].copy_(self.next_tok)
             self.vin[:, k + 1].copy_(self.next_tok)
             self.cur_pos.add_(1)
-        logits = self.step(K + 1, self.vin, self.pos0, verify=True)
-        torch.argmax(logits, dim=-1, out=self.argmax_buf)
+        self.step(K + 1, self.vin, self.pos0, verify=True)
+        self.argmax(K + 1, B * (K + 1), self.argmax_buf)
         self.vt.copy_(self.argmax_buf.view(B, K + 1))
         check(L.csaq_spec_accept(self.draft.data_ptr(), self.vt.data_ptr(), B, K, self.pos0.data_ptr(),
                                  self.out_tokens.data_ptr(), self.n_out.data_ptr(), self.cap,
@@ -294,8 +372,8 @@ class DecodeRuntime:
     def _greedy_step(self, verify: bool) -> None:
         L = lib()
         st = torch.cuda.current_stream(self.dev).cuda_stream
-        logits = self.step(1, self.next_tok, self.pos0, verify=verify)
-        torch.argmax(logits[: self.B], dim=-1, out=self.argmax_buf[: self.B])
+        self.step(1, self.next_tok, self.pos0, verify=verify)
+        self.argmax(1, self.B, self.argmax_buf[: self.B])
         check(L.csaq_greedy_commit(self.argmax_buf.data_ptr(), self.B, self.pos0.data_ptr(),
                                    self.out_tokens.data_ptr(), self.n_out.data_ptr(), self.cap,
                                    self.next_tok.data_ptr(), self.remaining.data_ptr(), st), "commit")

@@ -322,6 +322,71 @@ __global__ void silu_mul_kernel(const T* __restrict__ g, int64_t ldg, const T* _
   h[m * ldh + n] = from_f32<T>(sv * to_f32<T>(u[m * ldu + n]));
 }
 
+// ── tensor-parallel combine: out = T(out + sum_r parts[r]) in rank order ─────
+// parts: n_parts slices of (M, N) at part_stride elements apart, rows ld_p
+// apart; the fp32 sum runs over the ranks in order, so the result does not
+// depend on how many tokens share the call.
+template <typename T>
+__global__ void rank_sum_kernel(const T* __restrict__ parts, int n_parts, int64_t part_stride, int64_t ld_p,
+                                T* __restrict__ out, int64_t ldo, int64_t M, int N, int add_out) {
+  pdl_wait();
+  pdl_trigger();
+  const int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i >= M * N) return;
+  const int64_t m = i / N, n = i - m * N;
+  float v = add_out ? to_f32<T>(out[m * ldo + n]) : 0.0f;
+  for (int r = 0; r < n_parts; ++r) v = __fadd_rn(v, to_f32<T>(parts[r * part_stride + m * ld_p + n]));
+  out[m * ldo + n] = from_f32<T>(v);
+}
+
+// ── argmax over vocabulary slices ───────────────────────────────────────────
+// Row m of the logits is the concatenation of n_parts slices of part_len
+// values (slice r at part_stride * r, rows ld apart); idx[m] is the global
+// index of the largest value, the smallest such index on ties (as
+// torch.argmax). One CTA per row.
+constexpr int kArgThreads = 1024;
+
+template <typename T>
+__global__ void __launch_bounds__(kArgThreads) argmax_kernel(const T* __restrict__ logits, int n_parts,
+                                                             int64_t part_stride, int64_t ld, int64_t part_len,
+                                                             int64_t* __restrict__ idx) {
+  pdl_wait();
+  pdl_trigger();
+  const int64_t m = blockIdx.x;
+  float best = -INFINITY;
+  int64_t bi = INT64_MAX;
+  for (int r = 0; r < n_parts; ++r) {
+    const T* row = logits + r * part_stride + m * ld;
+    for (int64_t j = threadIdx.x; j < part_len; j += blockDim.x) {
+      const float v = to_f32<T>(row[j]);
+      const int64_t g = r * part_len + j;
+      if (v > best || (v == best && g < bi)) { best = v; bi = g; }
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float ov = __shfl_xor_sync(0xffffffffu, best, o);
+    const int64_t oi = __shfl_xor_sync(0xffffffffu, bi, o);
+    if (ov > best || (ov == best && oi < bi)) { best = ov; bi = oi; }
+  }
+  __shared__ float sv[32];
+  __shared__ int64_t si[32];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (lane == 0) { sv[warp] = best; si[warp] = bi; }
+  __syncthreads();
+  if (warp == 0) {
+    best = lane < (int)(blockDim.x >> 5) ? sv[lane] : -INFINITY;
+    bi = lane < (int)(blockDim.x >> 5) ? si[lane] : INT64_MAX;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float ov = __shfl_xor_sync(0xffffffffu, best, o);
+      const int64_t oi = __shfl_xor_sync(0xffffffffu, bi, o);
+      if (ov > best || (ov == best && oi < bi)) { best = ov; bi = oi; }
+    }
+    if (lane == 0) idx[m] = bi == INT64_MAX ? 0 : bi;
+  }
+}
+
 // ── greedy self-speculative acceptance ──────────────────────────────────────
 // Per sequence b: draft[b][0..K-1], verify argmax vt[b][0..K] (vt[k] follows
 // the context plus draft[0..k-1]). Accept the longest prefix with
@@ -479,6 +544,33 @@ extern "C" int csaq_greedy_commit(const int64_t* tok, int64_t B, int32_t* pos0, 
     return CSAQ_ERR_ARG;
   return launch_pdl(commit_kernel, dim3(blocks_for(B, 128)), dim3(128), 0, as_stream(stream), tok, (int)B,
                     pos0, out_tokens, n_out, (int)cap, next_tok, remaining);
+}
+
+extern "C" int csaq_rank_sum(const void* parts, int n_parts, int64_t part_stride, int64_t ld_parts, void* out,
+                             int64_t ldo, int64_t M, int64_t N, int add_out, int dtype, void* stream) {
+  if (!parts || !out || n_parts < 1 || M < 0 || N <= 0 || ld_parts < N || ldo < N) return CSAQ_ERR_ARG;
+  if (dtype != CSAQ_DT_F16 && dtype != CSAQ_DT_BF16) return CSAQ_ERR_ARG;
+  if (M == 0) return CSAQ_OK;
+  const dim3 grid((unsigned)((M * N + 255) / 256));
+  cudaStream_t st = as_stream(stream);
+  if (dtype == CSAQ_DT_BF16)
+    return launch_pdl(rank_sum_kernel<__nv_bfloat16>, grid, dim3(256), 0, st, (const __nv_bfloat16*)parts, n_parts,
+                      part_stride, ld_parts, (__nv_bfloat16*)out, ldo, M, (int)N, add_out);
+  return launch_pdl(rank_sum_kernel<__half>, grid, dim3(256), 0, st, (const __half*)parts, n_parts, part_stride,
+                    ld_parts, (__half*)out, ldo, M, (int)N, add_out);
+}
+
+extern "C" int csaq_argmax_parts(const void* logits, int n_parts, int64_t part_stride, int64_t ld,
+                                 int64_t part_len, int64_t M, int64_t* idx, int dtype, void* stream) {
+  if (!logits || !idx || n_parts < 1 || M < 0 || part_len <= 0 || ld < part_len) return CSAQ_ERR_ARG;
+  if (dtype != CSAQ_DT_F16 && dtype != CSAQ_DT_BF16) return CSAQ_ERR_ARG;
+  if (M == 0) return CSAQ_OK;
+  cudaStream_t st = as_stream(stream);
+  if (dtype == CSAQ_DT_BF16)
+    return launch_pdl(argmax_kernel<__nv_bfloat16>, dim3((unsigned)M), dim3(kArgThreads), 0, st,
+                      (const __nv_bfloat16*)logits, n_parts, part_stride, ld, part_len, idx);
+  return launch_pdl(argmax_kernel<__half>, dim3((unsigned)M), dim3(kArgThreads), 0, st, (const __half*)logits,
+                    n_parts, part_stride, ld, part_len, idx);
 }
 
 // ── csaq_decode_attention_static: decode attention with library-owned scratch

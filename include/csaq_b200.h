@@ -225,6 +225,20 @@ int csaq_decode_attention(const void* q, const void* k_cache, const void* v_cach
                           int64_t D, int64_t Lmax, float scale, float* part, int32_t* tickets,
                           void* out, int dtype, void* stream);
 
+/* Tensor-parallel combine: out[m, n] = T(out[m, n] (when add_out) + sum over
+ * r of parts[r*part_stride + m*ld_parts + n]), summed in fp32 in rank order.
+ * Replaces the all-reduce after the row-split o/down projections (the
+ * reference has no multi-GPU path; this is the combine step of its linears). */
+int csaq_rank_sum(const void* parts, int n_parts, int64_t part_stride, int64_t ld_parts, void* out,
+                  int64_t ldo, int64_t M, int64_t N, int add_out, int dtype, void* stream);
+
+/* Greedy token of each row: the global index of the largest logit over
+ * n_parts vocabulary slices of part_len values (slice r at r*part_stride,
+ * rows ld apart), the smallest index on ties; torch.argmax of the sampler
+ * at temperature 0 (csaq/inference.py:269-304). */
+int csaq_argmax_parts(const void* logits, int n_parts, int64_t part_stride, int64_t ld, int64_t part_len,
+                      int64_t M, int64_t* idx, int dtype, void* stream);
+
 /* csaq_decode_attention for callers that cannot allocate device memory: a
  * host-language binding that is handed raw device pointers (q, the caches,
  * pos0, out) by an application owning all device memory, or a

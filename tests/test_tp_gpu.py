@@ -1,0 +1,91 @@
+"""Tensor-parallel decode runtime on 2 GPUs (skipped with fewer).
+
+Two NCCL ranks run a quantised tiny Llama through DecodeRuntime with a TP
+group: the prefill logits match the single-GPU runtime's within 3e-2 (the
+partial sums are added in a different order), and greedy self-speculative
+output equals greedy decoding with the verify weights under TP.
+"""
+
+import os
+import socket
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _build(dev):
+    from csaq import _synthetic as syn
+    from csaq.config import CSAQConfig
+    from csaq.core import apply_csaq, solve_clique_budget
+    model = syn.build_decoder("tiny-llama", device=dev, seed=4, dtype=torch.bfloat16)
+    sal = syn.synthetic_salience(model, seed=5)
+    cfg = CSAQConfig(target_bits=4.0, bit_options=[4, 8, 16], group_size=128, protection_floor=0.10,
+                     clique_mode="per_channel")
+    cliques = {n: [[i] for i in range(s.shape[0])] for n, s in sal.items()}
+    budget, _, _ = solve_clique_budget(sal, cliques, cfg)
+    cmap = apply_csaq(model, budget, sal, cfg, verbose=False)
+    return model, cmap
+
+
+def _worker(rank, world, port, q):
+    import torch.distributed as dist
+    from datetime import timedelta
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    dev = torch.device("cuda", rank)
+    torch.cuda.set_device(dev)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=120), device_id=dev)
+    out = {}
+    try:
+        from csaq.runtime import DecodeRuntime
+        model, _ = _build(dev)
+        prompt = torch.randint(0, 2048, (1, 40), generator=torch.Generator().manual_seed(6)).to(dev)
+        rt = DecodeRuntime(model, 1, 256, 4, tp_group=dist.group.WORLD)
+        rt.reset(prompt, 24, verify=True)
+        out["tp_logits"] = rt.prefill_logits.float().cpu()
+        rt.generate_greedy(24, verify=True)
+        greedy = rt.outputs().cpu()
+        rt.reset(prompt, 24, verify=True)
+        rt.generate_speculative(24)
+        out["spec_equals_greedy"] = torch.equal(rt.outputs().cpu()[:, :24], greedy[:, :24])
+        rt.graphs.clear()
+        del rt
+        torch.cuda.synchronize()
+        if rank == 0:
+            one = DecodeRuntime(model, 1, 256, 4)
+            one.reset(prompt, 8, verify=True)
+            out["tp1_logits"] = one.prefill_logits.float().cpu()
+        dist.barrier()
+        q.put((rank, out))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_tensor_parallel_runtime_two_gpus():
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    import torch.multiprocessing as mp
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = dict(q.get(timeout=600) for _ in range(2))
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    for r in (0, 1):
+        assert res[r]["spec_equals_greedy"], r
+    a, b = res[0]["tp_logits"], res[0]["tp1_logits"]
+    assert torch.equal(res[0]["tp_logits"], res[1]["tp_logits"])
+    err = float((a - b).norm() / b.norm())
+    cos = float(torch.nn.functional.cosine_similarity(a.flatten(), b.flatten(), dim=0))
+    assert err < 3e-2 and cos > 0.999, (err, cos)
