@@ -195,9 +195,12 @@ class CausalProfiler:
     _EVAL_STRIDE: int = 8
     _SPEARMAN_SAMPLE: int = 50_000
 
-    def __init__(self, model: nn.Module, config: CSAQConfig) -> None:
+    def __init__(self, model: nn.Module, config: CSAQConfig, dp_group: Any = None) -> None:
         self.model = model
         self.config = config
+        # data parallel over calibration batches: rank r profiles batches r, r+W, ...;
+        # salience (fp32) and co-activation counts (int32) are summed over the ranks
+        self.dp_group = dp_group
         self.salience: SalienceMap = {}
         self._masks: Dict[str, MaskHistory] = {}
         self._hooks: List[Any] = []
@@ -233,8 +236,17 @@ class CausalProfiler:
             thr = float(torch.tensor(threshold, dtype=act.dtype)) if act.is_floating_point() else threshold
             mh.append(act, mode=0, thr=thr)
 
+    def _dp(self):
+        if self.dp_group is None:
+            return None, 0, 1
+        import torch.distributed as dist
+        return dist, dist.get_rank(self.dp_group), dist.get_world_size(self.dp_group)
+
     def profile(self, calib_data: List[Dict[str, torch.Tensor]],
                 verbose: bool = True) -> Tuple[SalienceMap, CliqueMap]:
+        dist, rank, world = self._dp()
+        if world > 1:
+            calib_data = list(calib_data)[rank::world]
         self.model.train()
         n_samples = len(calib_data)
         actual_batches = 0
@@ -263,9 +275,13 @@ class CausalProfiler:
             self.model.zero_grad()
             if (i + 1) % self._EVAL_STRIDE == 0 and (i + 1) >= self._EARLY_STOP_MIN_BATCHES:
                 all_s = torch.cat([self.salience[n].flatten().to(first_device) for n in self._modules])
+                if world > 1:  # every rank ranks the same (all-reduced) sample, so all stop together
+                    all_s = all_s.clone()
+                    dist.all_reduce(all_s, group=self.dp_group)
                 if eval_idx is None:
                     size = min(self._SPEARMAN_SAMPLE, all_s.numel())
-                    eval_idx = torch.randperm(all_s.numel(), device=all_s.device)[:size]
+                    gen = torch.Generator(device=all_s.device).manual_seed(0)
+                    eval_idx = torch.randperm(all_s.numel(), device=all_s.device, generator=gen)[:size]
                 ranks = all_s[eval_idx].argsort().argsort().float()
                 if prev_ranks is not None:
                     n_r = float(ranks.numel())
@@ -276,6 +292,12 @@ class CausalProfiler:
                             print(f"[CSAQ] Early stop at batch {i + 1}/{n_samples} (ρ={rho:.4f})")
                         break
                 prev_ranks = ranks.clone()
+        if world > 1:
+            n_b = torch.tensor([actual_batches], dtype=torch.int64, device=first_device)
+            dist.all_reduce(n_b, group=self.dp_group)
+            actual_batches = int(n_b)
+            for name in self.salience:
+                dist.all_reduce(self.salience[name], group=self.dp_group)
         for name in self.salience:
             acc = self.salience[name]
             check(lib().csaq_salience_finalize(acc.data_ptr(), acc.numel(), max(actual_batches, 1),
@@ -293,10 +315,14 @@ class CausalProfiler:
         for name, module in self._modules.items():
             mh = self._masks[name]
             C = module.weight.shape[0]
-            if mh.n_tok == 0:
+            if mh.n_tok == 0 and self.dp_group is None:
                 out[name] = [[i] for i in range(C)]
                 continue
             inter, f = coactivation_counts(mh.bits, mh.words_used())
+            dist, _, world = self._dp()
+            if world > 1:  # integer sums: every rank gets the same counts, hence the same cliques
+                dist.all_reduce(inter, group=self.dp_group)
+                dist.all_reduce(f, group=self.dp_group)
             out[name] = jaccard_cliques(inter, f, self.config.clique_threshold)
             del inter
             self._masks[name] = MaskHistory(C, mh.dev)
@@ -456,7 +482,7 @@ def apply_csaq(model: nn.Module, budget: BudgetMap, salience: SalienceMap, confi
 
 def quantize(model: nn.Module, calib_data, config: Optional[CSAQConfig] = None, verbose: bool = True,
              tokenizer: Any = None, seq_len: int = 128,
-             calibration_domain: str = "user_provided") -> Tuple[nn.Module, Dict[str, Any]]:
+             calibration_domain: str = "user_provided", dp_group: Any = None) -> Tuple[nn.Module, Dict[str, Any]]:
     """Full pipeline (csaq/core.py:425-553): profile -> solve -> apply."""
     if config is None:
         config = CSAQConfig()
@@ -487,7 +513,7 @@ def quantize(model: nn.Module, calib_data, config: Optional[CSAQConfig] = None, 
         return psutil.Process(os.getpid()).memory_info().rss / 1024 ** 3
 
     mem_before = _mem()
-    profiler = CausalProfiler(model, config)
+    profiler = CausalProfiler(model, config, dp_group=dp_group)
     salience, cliques = profiler.profile(calib, verbose=verbose)
     cliques_count = sum(len(v) for v in cliques.values())
     budget, tier_stats, actual_bits = solve_clique_budget(salience, cliques, config)

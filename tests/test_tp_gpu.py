@@ -89,3 +89,54 @@ def test_tensor_parallel_runtime_two_gpus():
     err = float((a - b).norm() / b.norm())
     cos = float(torch.nn.functional.cosine_similarity(a.flatten(), b.flatten(), dim=0))
     assert err < 3e-2 and cos > 0.999, (err, cos)
+
+
+def _dp_worker(rank, world, port, q):
+    import torch.distributed as dist
+    from datetime import timedelta
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    dev = torch.device("cuda", rank)
+    torch.cuda.set_device(dev)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=120), device_id=dev)
+    try:
+        from csaq import _synthetic as syn
+        from csaq.config import CSAQConfig
+        from csaq.core import CausalProfiler
+        model = syn.build_decoder("tiny-llama", device=dev, seed=0, dtype=torch.float32)
+        g = torch.Generator().manual_seed(3)
+        calib = [{"input_ids": torch.randint(0, 2048, (1, 32), generator=g)} for _ in range(4)]
+        cfg = CSAQConfig(clique_threshold=0.6, salience_alpha=1.0)
+        sal, cl = CausalProfiler(model, cfg, dp_group=dist.group.WORLD).profile(calib, verbose=False)
+        out = {"sal": {k: v.cpu() for k, v in sal.items()}, "cl": cl}
+        dist.barrier()
+        if rank == 0:
+            model.zero_grad()
+            sal1, cl1 = CausalProfiler(model, cfg).profile(calib, verbose=False)
+            out["sal1"] = {k: v.cpu() for k, v in sal1.items()}
+            out["cl1"] = cl1
+        q.put((rank, out))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_data_parallel_calibration_two_gpus():
+    """Two ranks profiling batches 0,2 and 1,3 give the single-GPU salience
+    (within 1e-3) and exactly the single-GPU cliques (integer count sums)."""
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    import torch.multiprocessing as mp
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_dp_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = dict(q.get(timeout=600) for _ in range(2))
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    r0, r1 = res[0], res[1]
+    assert r0["cl"] == r1["cl"] == r0["cl1"]
+    for k, v in r0["sal1"].items():
+        assert torch.equal(r0["sal"][k], r1["sal"][k]), k
+        assert torch.allclose(r0["sal"][k], v, rtol=1e-3, atol=1e-12), k
