@@ -65,6 +65,8 @@ _SIGNATURES = {
     "csaq_float_to_int": (c_int, [c_vp, c_vp, c_vp, c_int, c_i64, c_i64, c_vp, c_vp]),
     "csaq_dequant": (c_int, [c_vp, c_vp, c_vp, c_int, c_i64, c_i64, c_i64, c_int, c_int, c_vp, c_vp]),
     "csaq_qgemv_wait_timeouts": (c_int, [ctypes.POINTER(c_i64)]),
+    "csaq_qgemm": (c_int, [ctypes.POINTER(CsaqTier), c_int, c_i64, c_vp, c_int, c_i64, c_i64, c_vp]),
+    "csaq_qgemm_wait_timeouts": (c_int, [ctypes.POINTER(c_i64)]),
     "csaq_qgemv": (c_int, [ctypes.POINTER(CsaqTier), c_int, c_i64, c_vp, c_int, c_i64, c_i64, c_vp]),
     "csaq_qgemv_simt": (c_int, [ctypes.POINTER(CsaqTier), c_int, c_i64, c_vp, c_int, c_i64, c_i64, c_vp]),
     "csaq_tile_blocks_bytes": (c_i64, [c_int, c_i64, c_i64]),
@@ -182,3 +184,10 @@ def qgemv(descs, K: int, x: torch.Tensor, M: int, stream: int = None) -> None:
     arr = tier_array(descs) if isinstance(descs, list) else descs
     st = stream if stream is not None else stream_of(x)
     check(lib().csaq_qgemv(arr, len(descs), K, x.data_ptr(), dtype_code(x.dtype), M, x.stride(0), st), "qgemv")
+
+
+def qgemm(descs, K: int, x: torch.Tensor, M: int, stream: int = None) -> None:
+    """Launch csaq_qgemm (the many-token tensor-core path) on tier descriptors."""
+    arr = tier_array(descs) if isinstance(descs, list) else descs
+    st = stream if stream is not None else stream_of(x)
+    check(lib().csaq_qgemm(arr, len(descs), K, x.data_ptr(), dtype_code(x.dtype), M, x.stride(0), st), "qgemm")

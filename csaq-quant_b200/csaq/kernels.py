@@ -300,6 +300,11 @@ def inject_csaq_linear(model: nn.Module, budget: dict, verbose: bool = True) -> 
 # CSAQLinear
 # ─────────────────────────────────────────────────────────────────────────────
 
+# From this many tokens on, forward() uses the tcgen05 dequantise-GEMM (csaq_qgemm)
+# instead of the decode GEMV (which re-reads the weights once per 16 tokens).
+GEMM_MIN_TOKENS = 32
+
+
 class _Tier:
     """One row tier as the GEMV reads it (kept alive for the ctypes descriptors)."""
 
@@ -783,7 +788,10 @@ class CSAQLinear(nn.Module):
         y = torch.empty(M, N, dtype=x2.dtype, device=x2.device)
         if M:
             descs = self.gemv_descriptors(y, verify=self.verify_mode)
-            _lib.qgemv(descs, K, x2, M)
+            if M >= GEMM_MIN_TOKENS and K % 64 == 0 and x2.dtype in (torch.float16, torch.bfloat16):
+                _lib.qgemm(descs, K, x2, M)   # many tokens: the tensor-core GEMM
+            else:
+                _lib.qgemv(descs, K, x2, M)
         y = y.view(*x.shape[:-1], N)
         return y if y.device == dev else y.to(dev)
 

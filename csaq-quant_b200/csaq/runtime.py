@@ -39,6 +39,11 @@ from . import _lib
 from ._lib import check, dtype_code, lib, ptr
 from .kernels import CSAQLinear
 
+# Prefill chunks of at least this many tokens use the tcgen05 GEMM; smaller
+# steps (decode, verify, the default 64-token prefill chunks) use the GEMV,
+# which is faster there.
+RUNTIME_GEMM_MIN_TOKENS = 256
+
 
 def _layers_of(model: nn.Module):
     inner = getattr(model, "model", None)
@@ -222,8 +227,13 @@ class DecodeRuntime:
 
     # ── one step of S tokens per sequence ───────────────────────────────────
     def _gemv(self, arr_n, K: int, x: torch.Tensor, M: int, st: int) -> None:
+        """One quantised linear launch: the decode GEMV for a few tokens, the
+        tcgen05 GEMM for prefill chunks of RUNTIME_GEMM_MIN_TOKENS tokens or more."""
         arr, n = arr_n
-        check(lib().csaq_qgemv(arr, n, K, x.data_ptr(), self.dt, M, x.stride(0), st), "qgemv")
+        if M >= RUNTIME_GEMM_MIN_TOKENS and K % 64 == 0:
+            check(lib().csaq_qgemm(arr, n, K, x.data_ptr(), self.dt, M, x.stride(0), st), "qgemm")
+        else:
+            check(lib().csaq_qgemv(arr, n, K, x.data_ptr(), self.dt, M, x.stride(0), st), "qgemv")
 
     def _combine(self, sh: _Shape, M: int, st: int) -> None:
         """TP: gather every rank's partial o/down output and add them to x in rank order."""

@@ -149,6 +149,20 @@ int csaq_repack_tiles(const csaq_tier* tier, int64_t K, uint8_t* blocks, void* s
 int csaq_qgemv(const csaq_tier* tiers, int n_tiers, int64_t K, const void* x, int x_dtype,
                int64_t M, int64_t ldx, void* stream);
 
+/* The same product for many tokens (prefill / verify with M in the tens to
+ * thousands), on the tcgen05 tensor cores: X (bf16 or fp16) times the tier
+ * weights dequantised in shared memory to X's dtype, exactly as the
+ * reference's forward materialises them (csaq/kernels.py:450-475: fp32
+ * (q - zp) * s, then .to(x.dtype)), fp32 accumulation in tensor memory.
+ * Reads the reference layout (`codes`, `scales`, `zps`; `blocks` unused).
+ * Needs K % 64 == 0, 16-byte aligned x with ldx % 8 == 0, group sizes that
+ * are multiples of 64, and code rows (pointer and row_bytes) aligned to 16
+ * bytes (8 for 2-bit tiers) (else CSAQ_ERR_UNSUPPORTED). One launch per tier. */
+int csaq_qgemm(const csaq_tier* tiers, int n_tiers, int64_t K, const void* x, int x_dtype, int64_t M,
+               int64_t ldx, void* stream);
+/* CTAs of csaq_qgemm whose bounded wait for the tensor core gave up (diagnostic). */
+int csaq_qgemm_wait_timeouts(int64_t* count);
+
 /* Number of warps, since the library was loaded on this device, whose bounded
  * wait for a weight copy in the tensor-core kernel gave up (the launch still
  * ends; its output is then unreliable). Synchronises the device. No

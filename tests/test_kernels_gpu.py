@@ -326,6 +326,79 @@ def test_qgemv_no_abandoned_waits():
     assert n.value == 0
 
 
+@pytest.mark.parametrize("m,n,k", [(32, 300, 512), (130, 256, 4096), (512, 1100, 1024)])
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+def test_qgemm_matches_oracle(m, n, k, dtype):
+    """The tcgen05 GEMM (M >= 32) against the oracle: within 1e-2 of the fp32
+    dequant-then-matmul, and within the output dtype's rounding of the
+    reference's own numerics (weights rounded to x.dtype before the matmul)."""
+    from csaq import _lib
+    layer, case, _ = _mixed_layer(n, k, seed=m + k, dtype=dtype, bias=True)
+    Wref = _oracle_mixed(case)
+    x = torch.randn(m, k, generator=torch.Generator().manual_seed(m)).to(dtype)
+    r = torch.randn(m, n, generator=torch.Generator().manual_seed(m + 1)).to(dtype)
+    y = r.clone().to(DEV)
+    d = layer.gemv_descriptors(y, residual=y)
+    _lib.qgemm(d, k, x.to(DEV), m)
+    got = y.float().cpu().numpy()
+    bias = layer.bias.float().cpu().numpy()
+    ref = O.linear_ref(x.float().numpy(), Wref, bias) + r.float().numpy()
+    assert_linear_close(got, ref, what=f"qgemm {m}x{n}x{k} {dtype}")
+    Wx = torch.from_numpy(Wref).to(dtype).float().numpy()   # the reference rounds W to x.dtype
+    ref_x = O.linear_ref(x.float().numpy(), Wx, bias) + r.float().numpy()
+    tight = 4e-3 if dtype == torch.bfloat16 else 2e-3        # the output's own rounding: 2^-8 / 2^-11
+    assert_linear_close(got, ref_x, rtol=tight, what=f"qgemm (x-dtype weights) {m}x{n}x{k}")
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+def test_qgemm_low_bit_tiers(dtype):
+    """8/4/2-bit tiers (the 70B prefill mix), group 256, ragged M and rows."""
+    from csaq import _lib
+    layer, case, _ = _mixed_layer(600, 1024, seed=7, dtype=dtype, bits=(8, 4, 2), fracs=(0.1, 0.6),
+                                  group_size=256)
+    Wref = _oracle_mixed(case, group_size=256)
+    for m in (40, 300):
+        x = torch.randn(m, 1024, generator=torch.Generator().manual_seed(m)).to(dtype)
+        y = torch.zeros(m, 600, dtype=dtype, device=DEV)
+        _lib.qgemm(layer.gemv_descriptors(y), 1024, x.to(DEV), m)
+        got = y.float().cpu().numpy()
+        assert_linear_close(got, O.linear_ref(x.float().numpy(), Wref), what=f"qgemm 8/4/2 m={m}")
+        Wx = torch.from_numpy(Wref).to(dtype).float().numpy()
+        tight = 4e-3 if dtype == torch.bfloat16 else 2e-3
+        assert_linear_close(got, O.linear_ref(x.float().numpy(), Wx), rtol=tight, what=f"qgemm 8/4/2 x-dtype m={m}")
+
+
+def test_qgemm_token_result_independent_of_m():
+    """A token's GEMM output is bitwise the same for any M (tiles split tokens,
+    never the K accumulation)."""
+    from csaq import _lib
+    layer, _, _ = _mixed_layer(520, 1024, seed=11, dtype=torch.bfloat16)
+    x = torch.randn(300, 1024, generator=torch.Generator().manual_seed(2)).to(torch.bfloat16).to(DEV)
+    outs = {}
+    for m in (33, 140, 300):
+        y = torch.zeros(m, 520, dtype=torch.bfloat16, device=DEV)
+        _lib.qgemm(layer.gemv_descriptors(y), 1024, x[:m], m)
+        outs[m] = y
+    assert torch.equal(outs[33], outs[300][:33])
+    assert torch.equal(outs[140], outs[300][:140])
+
+
+def test_qgemm_forward_dispatch_and_no_timeouts():
+    """CSAQLinear.forward takes the GEMM from 32 tokens on; it agrees with the GEMV."""
+    import ctypes
+    from csaq import _lib
+    from csaq._lib import check, lib
+    layer, _, _ = _mixed_layer(512, 1024, seed=5, dtype=torch.bfloat16)
+    x = torch.randn(48, 1024, generator=torch.Generator().manual_seed(2)).to(torch.bfloat16).to(DEV)
+    y_gemm = layer(x)
+    y_gemv = torch.empty_like(y_gemm)
+    _lib.qgemv(layer.gemv_descriptors(y_gemv), 1024, x, 48)
+    assert_linear_close(y_gemm.float().cpu().numpy(), y_gemv.float().cpu().numpy(), what="gemm vs gemv")
+    n = ctypes.c_int64(-1)
+    check(lib().csaq_qgemm_wait_timeouts(ctypes.byref(n)), "timeouts")
+    assert n.value == 0
+
+
 def test_uniform_layer_ragged_shapes():
     """K = 37 (no 128-column chunks): the CUDA-core kernel serves it."""
     from csaq.kernels import CSAQLinear
