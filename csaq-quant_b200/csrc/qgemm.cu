@@ -23,8 +23,9 @@
 //     columns 0-255, tokens 128-255 at columns 256-511); each step's commit
 //     frees its load stage and its B buffer;
 //   * after the last step warps 2-9 read the accumulators with tcgen05.ld
-//     (a warp reads the 32 lanes its rank allows), add bias and residual and
-//     scatter the rows to their output columns.
+//     (a warp reads the 32 lanes its rank allows), turn each 32 x 32 block
+//     around in shared memory, add bias and residual and store the rows to
+//     their output columns, one token per store instruction.
 // Tiles are visited in groups of 8 token tiles, so the CTAs running at once
 // share their activation and weight tiles through L2. Tokens beyond M and
 // rows beyond the tier read as zeros. Every wait is bounded; a CTA whose wait
@@ -150,9 +151,15 @@ __device__ __forceinline__ uint32_t raw_off(int rb, int r, int i) {
   return a ^ (((a >> 7) & mask) << 4);
 }
 
+// a and b rounded to the activation dtype, a in the low half
 template <typename ACT>
 __device__ __forceinline__ uint32_t pack2(float a, float b) {
-  return bits_of<ACT>(from_f32<ACT>(a)) | (bits_of<ACT>(from_f32<ACT>(b)) << 16);
+  uint32_t d;
+  if (std::is_same<ACT, __nv_bfloat16>::value)
+    asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(d) : "f"(b), "f"(a));
+  else
+    asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(d) : "f"(b), "f"(a));
+  return d;
 }
 
 // 2^23 + (byte `byte` of w), exactly, as fp32
@@ -160,18 +167,21 @@ __device__ __forceinline__ float magic(uint32_t w, uint32_t byte) {
   return __uint_as_float(__byte_perm(w, 0x4B000000u, 0x7440u | byte));
 }
 
-// (q - zp) * s of the four codes in the bytes of w (code j in byte j), as two
-// packed pairs; c = 2^23 + zp
+// one packed pair (q_a - zp) * s, (q_b - zp) * s from the codes in byte
+// `byte` of wa and of wb; nc = -(2^23 + zp) and ss = s in both lanes (the
+// packed fp32 add and multiply round each lane like the scalar ops)
 template <typename ACT>
-__device__ __forceinline__ uint2 dq4(uint32_t w, float c, float s) {
-  return make_uint2(pack2<ACT>(__fmul_rn(__fsub_rn(magic(w, 0), c), s), __fmul_rn(__fsub_rn(magic(w, 1), c), s)),
-                    pack2<ACT>(__fmul_rn(__fsub_rn(magic(w, 2), c), s), __fmul_rn(__fsub_rn(magic(w, 3), c), s)));
+__device__ __forceinline__ uint32_t dq2(uint32_t wa, uint32_t wb, uint32_t byte, float2 nc, float2 ss) {
+  const float2 d = __fmul2_rn(__fadd2_rn(make_float2(magic(wa, byte), magic(wb, byte)), nc), ss);
+  return pack2<ACT>(d.x, d.y);
 }
 
-// one packed pair: the codes in byte `byte` of wa (first) and of wb (second)
+// the four codes in the bytes of w (code j in byte j) as two packed pairs
 template <typename ACT>
-__device__ __forceinline__ uint32_t dq2(uint32_t wa, uint32_t wb, uint32_t byte, float c, float s) {
-  return pack2<ACT>(__fmul_rn(__fsub_rn(magic(wa, byte), c), s), __fmul_rn(__fsub_rn(magic(wb, byte), c), s));
+__device__ __forceinline__ uint2 dq4(uint32_t w, float2 nc, float2 ss) {
+  const float2 d0 = __fmul2_rn(__fadd2_rn(make_float2(magic(w, 0), magic(w, 1)), nc), ss);
+  const float2 d1 = __fmul2_rn(__fadd2_rn(make_float2(magic(w, 2), magic(w, 3)), nc), ss);
+  return make_uint2(pack2<ACT>(d0.x, d0.y), pack2<ACT>(d1.x, d1.y));
 }
 
 // Dequantise one weight row's 64 codes of a step (raw tile `tile`, row r) and
@@ -180,6 +190,7 @@ template <typename ACT>
 __device__ __forceinline__ void dequant_row(int bits, const uint8_t* tile, int r, float c, float s, uint8_t* brow,
                                             bool live) {
   const int rb = raw_row_bytes(bits);
+  const float2 nc = make_float2(-c, -c), ss = make_float2(s, s);
   uint4 out[8];
   if (!live) {
 #pragma unroll
@@ -188,8 +199,8 @@ __device__ __forceinline__ void dequant_row(int bits, const uint8_t* tile, int r
 #pragma unroll
     for (int i = 0; i < 4; ++i) {  // 16 codes a chunk: output chunks 2i, 2i+1
       const uint4 q = *reinterpret_cast<const uint4*>(tile + raw_off(rb, r, i));
-      const uint2 a = dq4<ACT>(q.x, c, s), b = dq4<ACT>(q.y, c, s), e = dq4<ACT>(q.z, c, s),
-                  f = dq4<ACT>(q.w, c, s);
+      const uint2 a = dq4<ACT>(q.x, nc, ss), b = dq4<ACT>(q.y, nc, ss), e = dq4<ACT>(q.z, nc, ss),
+                  f = dq4<ACT>(q.w, nc, ss);
       out[2 * i] = make_uint4(a.x, a.y, b.x, b.y);
       out[2 * i + 1] = make_uint4(e.x, e.y, f.x, f.y);
     }
@@ -201,8 +212,8 @@ __device__ __forceinline__ void dequant_row(int bits, const uint8_t* tile, int r
 #pragma unroll
       for (int j = 0; j < 4; ++j) {  // word j: code 2t + h of its 8 in nibble h of byte t
         const uint32_t lo = w[j] & 0x0F0F0F0Fu, hi = (w[j] >> 4) & 0x0F0F0F0Fu;
-        out[4 * i + j] = make_uint4(dq2<ACT>(lo, hi, 0, c, s), dq2<ACT>(lo, hi, 1, c, s),
-                                    dq2<ACT>(lo, hi, 2, c, s), dq2<ACT>(lo, hi, 3, c, s));
+        out[4 * i + j] = make_uint4(dq2<ACT>(lo, hi, 0, nc, ss), dq2<ACT>(lo, hi, 1, nc, ss),
+                                    dq2<ACT>(lo, hi, 2, nc, ss), dq2<ACT>(lo, hi, 3, nc, ss));
       }
     }
   } else if (bits == 2) {
@@ -212,10 +223,10 @@ __device__ __forceinline__ void dequant_row(int bits, const uint8_t* tile, int r
     for (int j = 0; j < 4; ++j) {  // word j: code 4t + h of its 16 in bits 2h of byte t
       const uint32_t m0 = w[j] & 0x03030303u, m1 = (w[j] >> 2) & 0x03030303u, m2 = (w[j] >> 4) & 0x03030303u,
                      m3 = (w[j] >> 6) & 0x03030303u;
-      out[2 * j] = make_uint4(dq2<ACT>(m0, m1, 0, c, s), dq2<ACT>(m2, m3, 0, c, s), dq2<ACT>(m0, m1, 1, c, s),
-                              dq2<ACT>(m2, m3, 1, c, s));
-      out[2 * j + 1] = make_uint4(dq2<ACT>(m0, m1, 2, c, s), dq2<ACT>(m2, m3, 2, c, s),
-                                  dq2<ACT>(m0, m1, 3, c, s), dq2<ACT>(m2, m3, 3, c, s));
+      out[2 * j] = make_uint4(dq2<ACT>(m0, m1, 0, nc, ss), dq2<ACT>(m2, m3, 0, nc, ss), dq2<ACT>(m0, m1, 1, nc, ss),
+                              dq2<ACT>(m2, m3, 1, nc, ss));
+      out[2 * j + 1] = make_uint4(dq2<ACT>(m0, m1, 2, nc, ss), dq2<ACT>(m2, m3, 2, nc, ss),
+                                  dq2<ACT>(m0, m1, 3, nc, ss), dq2<ACT>(m2, m3, 3, nc, ss));
     }
   } else {  // fp16 rows: 8 values a chunk
 #pragma unroll
@@ -349,26 +360,23 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int r = tid - 64;
     const int64_t wrow = row0 + r;
     const bool live = wrow < T.n_rows;
-    // scale and 2^23 + zero point of step k, fetched two steps before their use
-    auto load_sz = [&](int k, float& c, float& sc) {
-      c = 8388608.0f;
+    // scale and zero point of step k (raw: nothing waits on the loads here)
+    auto load_sz = [&](int k, uint32_t& z, float& sc) {
+      z = 0u;
       sc = 0.0f;
       if (live && bits != 16 && k < n_k) {
         const int64_t gi = wrow * T.n_groups + (T.n_groups > 1 ? ((int64_t)k * kBK) / T.group_size : 0);
         sc = T.scales[gi];
-        c = 8388608.0f + (float)T.zps[gi];
+        z = T.zps[gi];
       }
     };
-    float c0, s0, c1, s1, c2, s2;
-    load_sz(0, c0, s0);
-    load_sz(1, c1, s1);
     int s = 0, sb = 0;
     uint32_t ph = 0, phb = 0;
-    for (int kt = 0; kt < n_k; ++kt) {
-      load_sz(kt + 2, c2, s2);
-      if (!mbar_wait(full + 8 * s, ph, abort_flag)) break;
-      if (!mbar_wait(bempty + 8 * sb, phb ^ 1u, abort_flag)) break;
-      dequant_row<ACT>(bits, gbase + (w_ring - base) + s * w_tile, r, c0, s0,
+    // one step: wait for the stage's codes and a free B buffer, dequantise, publish
+    auto step = [&](int kt, uint32_t z, float sc) -> bool {
+      if (!mbar_wait(full + 8 * s, ph, abort_flag)) return false;
+      if (!mbar_wait(bempty + 8 * sb, phb ^ 1u, abort_flag)) return false;
+      dequant_row<ACT>(bits, gbase + (w_ring - base) + s * w_tile, r, 8388608.0f + (float)z, sc,
                        gbase + (b_ring - base) + sb * kBTile + r * 128, live);
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // generic writes -> tensor core
       __syncwarp();
@@ -378,41 +386,69 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       if (++s == n_ls) { s = 0; ph ^= 1u; }
       if (++sb == kBBufs) { sb = 0; phb ^= 1u; }
-      c0 = c1; s0 = s1;
-      c1 = c2; s1 = s2;
+      return true;
+    };
+    // two steps a trip, each with its own scale registers, refilled for two
+    // steps later right after use: the loads have a step to land and no
+    // register copy waits on them
+    uint32_t za, zb;
+    float sa, sb2;
+    load_sz(0, za, sa);
+    load_sz(1, zb, sb2);
+    for (int kt = 0; kt < n_k; kt += 2) {
+      if (!step(kt, za, sa)) break;
+      load_sz(kt + 2, za, sa);
+      if (kt + 1 < n_k) {
+        if (!step(kt + 1, zb, sb2)) break;
+        load_sz(kt + 3, zb, sb2);
+      }
     }
 
     // ── epilogue: warp w reads TMEM lanes 32 (w % 4) .. +31 of accumulator (w - 2) / 4 ──
+    // 32 x 32 blocks pass through shared memory (the A ring, idle once every
+    // MMA is done), so that a store instruction writes one token's 32
+    // consecutive tier rows (ascending output columns) rather than 32 tokens'
+    // rows of one column.
     volatile int never = 0;
     const bool done = mbar_wait(accfull, 0u, &never) && !*abort_flag;
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
     const int q = warp & 3, half = (warp - 2) >> 2;
-    const int64_t tok = tok0 + 128 * half + 32 * q + lane;
-    if (done && (half == 0 || two)) {
+    const int64_t tokw = tok0 + 128 * half + 32 * q;  // this warp's first token
+    float* buf = reinterpret_cast<float*>(gbase) + (warp - 2) * (32 * 33);
+    if (done && (half == 0 || two) && tokw < M) {
 #pragma unroll 1
-      for (int cb = 0; cb < kBN; cb += 16) {
-        uint32_t v[16];
+      for (int cb = 0; cb < kBN && row0 + cb < T.n_rows; cb += 32) {
+        uint32_t v[32];
         const uint32_t taddr = tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)(256 * half + cb);
         asm volatile(
-            "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+            "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+            "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
             : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]),
               "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]),
-              "=r"(v[15])
+              "=r"(v[15]), "=r"(v[16]), "=r"(v[17]), "=r"(v[18]), "=r"(v[19]), "=r"(v[20]), "=r"(v[21]),
+              "=r"(v[22]), "=r"(v[23]), "=r"(v[24]), "=r"(v[25]), "=r"(v[26]), "=r"(v[27]), "=r"(v[28]),
+              "=r"(v[29]), "=r"(v[30]), "=r"(v[31])
             : "r"(taddr));
         asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-        if (tok < M) {
 #pragma unroll
-          for (int j = 0; j < 16; ++j) {
-            const int row = row0 + cb + j;
-            if (row >= T.n_rows) break;
-            float y = __uint_as_float(v[j]);
-            const int orow = T.out_rows[row];
-            if (T.bias) y = __fadd_rn(y, to_f32<ACT>(reinterpret_cast<const ACT*>(T.bias)[orow]));
+        for (int j = 0; j < 32; ++j) buf[lane * 33 + j] = __uint_as_float(v[j]);  // [token][row]
+        __syncwarp();
+        const int row = row0 + cb + lane;  // lane = tier row
+        const bool rlive = row < T.n_rows;
+        const int orow = rlive ? T.out_rows[row] : 0;
+        const float bv = (rlive && T.bias) ? to_f32<ACT>(reinterpret_cast<const ACT*>(T.bias)[orow]) : 0.0f;
+        const int nt_w = M - tokw < 32 ? (int)(M - tokw) : 32;
+        for (int t = 0; t < nt_w; ++t) {
+          const int64_t tok = tokw + t;
+          float y = buf[t * 33 + lane];
+          if (rlive) {
+            if (T.bias) y = __fadd_rn(y, bv);
             if (T.residual)
               y = __fadd_rn(y, to_f32<ACT>(reinterpret_cast<const ACT*>(T.residual)[tok * T.ldr + orow]));
             reinterpret_cast<ACT*>(T.y)[tok * T.ldy + orow] = from_f32<ACT>(y);
           }
         }
+        __syncwarp();
       }
     }
   }
