@@ -45,12 +45,13 @@ namespace {
 constexpr int kBM = 256;                   // tokens per tile (two MMAs of M = 128)
 constexpr int kBN = 256;                   // weight rows per tile (MMA N)
 constexpr int kBK = 64;                    // columns per step (one 128-byte swizzle row of bf16)
-constexpr int kThreads = 320;              // warp 0 TMA, warp 1 MMA, warps 2-9 dequantise + epilogue
-constexpr int kDqWarps = 8;
+constexpr int kDqWarps = 16;               // two threads a weight row
+constexpr int kThreads = 64 + 32 * kDqWarps;  // warp 0 TMA, warp 1 MMA, warps 2-17 dequantise + epilogue
 constexpr int kATile = kBM * kBK * 2;      // 32 KB
 constexpr int kBTile = kBN * kBK * 2;      // 32 KB
 constexpr int kBBufs = 2;
 constexpr int kMaxSmem = 232448;           // dynamic shared memory a CTA may opt into
+constexpr int kEpiBytes = kDqWarps * 32 * 33 * 4;  // epilogue transpose blocks (in the rings)
 constexpr int kGroupM = 8;                 // token tiles per raster group
 constexpr int kWait = 1 << 22;             // polls of an mbarrier before a wait gives up
 
@@ -63,6 +64,9 @@ __host__ __device__ constexpr int smem_bytes(int bits) {
 static_assert(smem_bytes(2) <= kMaxSmem && smem_bytes(4) <= kMaxSmem && smem_bytes(8) <= kMaxSmem &&
                   smem_bytes(16) <= kMaxSmem,
               "stage ring exceeds shared memory");
+static_assert(2 * (kATile + kBN * raw_row_bytes(16)) >= kEpiBytes && 3 * (kATile + kBN * raw_row_bytes(8)) >= kEpiBytes &&
+                  4 * (kATile + kBN * raw_row_bytes(2)) >= kEpiBytes,
+              "epilogue blocks exceed the rings");
 
 __device__ unsigned int g_qgemm_timeouts;
 
@@ -184,43 +188,40 @@ __device__ __forceinline__ uint2 dq4(uint32_t w, float2 nc, float2 ss) {
   return make_uint2(pack2<ACT>(d0.x, d0.y), pack2<ACT>(d1.x, d1.y));
 }
 
-// Dequantise one weight row's 64 codes of a step (raw tile `tile`, row r) and
-// store them as the 8 swizzled 16-byte chunks of B row r at `brow`.
-template <typename ACT>
-__device__ __forceinline__ void dequant_row(int bits, const uint8_t* tile, int r, float c, float s, uint8_t* brow,
-                                            bool live) {
-  const int rb = raw_row_bytes(bits);
+// Dequantise half h (columns 32h .. 32h+31) of weight row r of a step from
+// the raw tile and store it as chunks 4h .. 4h+3 of B row r (at brow).
+template <typename ACT, int BITS>
+__device__ __forceinline__ void dequant_half(const uint8_t* tile, int r, int h, float c, float s, uint8_t* brow,
+                                             bool live) {
+  constexpr int rb = raw_row_bytes(BITS);
   const float2 nc = make_float2(-c, -c), ss = make_float2(s, s);
-  uint4 out[8];
+  uint4 out[4];
   if (!live) {
 #pragma unroll
-    for (int k = 0; k < 8; ++k) out[k] = make_uint4(0u, 0u, 0u, 0u);
-  } else if (bits == 8) {
+    for (int k = 0; k < 4; ++k) out[k] = make_uint4(0u, 0u, 0u, 0u);
+  } else if (BITS == 8) {
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {  // 16 codes a chunk: output chunks 2i, 2i+1
-      const uint4 q = *reinterpret_cast<const uint4*>(tile + raw_off(rb, r, i));
+    for (int i = 0; i < 2; ++i) {  // chunk 2h + i: 16 codes, output chunks 2i, 2i + 1 of the half
+      const uint4 q = *reinterpret_cast<const uint4*>(tile + raw_off(rb, r, 2 * h + i));
       const uint2 a = dq4<ACT>(q.x, nc, ss), b = dq4<ACT>(q.y, nc, ss), e = dq4<ACT>(q.z, nc, ss),
                   f = dq4<ACT>(q.w, nc, ss);
       out[2 * i] = make_uint4(a.x, a.y, b.x, b.y);
       out[2 * i + 1] = make_uint4(e.x, e.y, f.x, f.y);
     }
-  } else if (bits == 4) {
-#pragma unroll
-    for (int i = 0; i < 2; ++i) {  // 32 codes a chunk: output chunks 4i .. 4i+3
-      const uint4 q = *reinterpret_cast<const uint4*>(tile + raw_off(rb, r, i));
-      const uint32_t w[4] = {q.x, q.y, q.z, q.w};
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {  // word j: code 2t + h of its 8 in nibble h of byte t
-        const uint32_t lo = w[j] & 0x0F0F0F0Fu, hi = (w[j] >> 4) & 0x0F0F0F0Fu;
-        out[4 * i + j] = make_uint4(dq2<ACT>(lo, hi, 0, nc, ss), dq2<ACT>(lo, hi, 1, nc, ss),
-                                    dq2<ACT>(lo, hi, 2, nc, ss), dq2<ACT>(lo, hi, 3, nc, ss));
-      }
-    }
-  } else if (bits == 2) {
-    const uint4 q = *reinterpret_cast<const uint4*>(tile + raw_off(rb, r, 0));
+  } else if (BITS == 4) {
+    const uint4 q = *reinterpret_cast<const uint4*>(tile + raw_off(rb, r, h));  // 32 codes
     const uint32_t w[4] = {q.x, q.y, q.z, q.w};
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {  // word j: code 4t + h of its 16 in bits 2h of byte t
+    for (int j = 0; j < 4; ++j) {  // word j: code 2t + n of its 8 in nibble n of byte t
+      const uint32_t lo = w[j] & 0x0F0F0F0Fu, hi = (w[j] >> 4) & 0x0F0F0F0Fu;
+      out[j] = make_uint4(dq2<ACT>(lo, hi, 0, nc, ss), dq2<ACT>(lo, hi, 1, nc, ss), dq2<ACT>(lo, hi, 2, nc, ss),
+                          dq2<ACT>(lo, hi, 3, nc, ss));
+    }
+  } else if (BITS == 2) {
+    const uint2 q = *reinterpret_cast<const uint2*>(tile + raw_off(rb, r, 0) + 8 * h);  // 32 codes
+    const uint32_t w[2] = {q.x, q.y};
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {  // word j: code 4t + n of its 16 in bits 2n of byte t
       const uint32_t m0 = w[j] & 0x03030303u, m1 = (w[j] >> 2) & 0x03030303u, m2 = (w[j] >> 4) & 0x03030303u,
                      m3 = (w[j] >> 6) & 0x03030303u;
       out[2 * j] = make_uint4(dq2<ACT>(m0, m1, 0, nc, ss), dq2<ACT>(m2, m3, 0, nc, ss), dq2<ACT>(m0, m1, 1, nc, ss),
@@ -228,10 +229,10 @@ __device__ __forceinline__ void dequant_row(int bits, const uint8_t* tile, int r
       out[2 * j + 1] = make_uint4(dq2<ACT>(m0, m1, 2, nc, ss), dq2<ACT>(m2, m3, 2, nc, ss),
                                   dq2<ACT>(m0, m1, 3, nc, ss), dq2<ACT>(m2, m3, 3, nc, ss));
     }
-  } else {  // fp16 rows: 8 values a chunk
+  } else {  // fp16 rows: chunk 4h + i holds 8 values
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      const uint4 q = *reinterpret_cast<const uint4*>(tile + raw_off(rb, r, i));
+    for (int i = 0; i < 4; ++i) {
+      const uint4 q = *reinterpret_cast<const uint4*>(tile + raw_off(rb, r, 4 * h + i));
       if (std::is_same<ACT, __half>::value) {
         out[i] = q;
       } else {
@@ -246,19 +247,18 @@ __device__ __forceinline__ void dequant_row(int bits, const uint8_t* tile, int r
     }
   }
 #pragma unroll
-  for (int k = 0; k < 8; ++k) *reinterpret_cast<uint4*>(brow + ((k ^ (r & 7)) << 4)) = out[k];
+  for (int k = 0; k < 4; ++k) *reinterpret_cast<uint4*>(brow + (((4 * h + k) ^ (r & 7)) << 4)) = out[k];
 }
 
-template <typename ACT>
+template <typename ACT, int BITS>
 __global__ void __launch_bounds__(kThreads, 1)
     qgemm_kernel(const __grid_constant__ CUtensorMap map_x, const __grid_constant__ CUtensorMap map_w,
                  const csaq_tier T, int64_t K, int64_t M) {
   extern __shared__ __align__(16) uint8_t smem_raw[];
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int bits = T.bits;
-  const int n_ls = load_stages(bits);
-  const int rb = raw_row_bytes(bits);
-  const int w_tile = kBN * rb;
+  constexpr int n_ls = load_stages(BITS);
+  constexpr int rb = raw_row_bytes(BITS);
+  constexpr int w_tile = kBN * rb;
 
   // grouped raster: kGroupM token tiles x every row tile, token tile fastest
   const int n_m = (int)((M + kBM - 1) / kBM), n_n = (T.n_rows + kBN - 1) / kBN;
@@ -356,15 +356,15 @@ __global__ void __launch_bounds__(kThreads, 1)
       mma_commit(accfull);  // completes when every MMA issued above has
     }
   } else {
-    // ── dequantise: one weight row a thread ──
-    const int r = tid - 64;
+    // ── dequantise: two threads a weight row ──
+    const int d = tid - 64, r = d >> 1, h = d & 1;
     const int64_t wrow = row0 + r;
     const bool live = wrow < T.n_rows;
     // scale and zero point of step k (raw: nothing waits on the loads here)
     auto load_sz = [&](int k, uint32_t& z, float& sc) {
       z = 0u;
       sc = 0.0f;
-      if (live && bits != 16 && k < n_k) {
+      if (live && BITS != 16 && k < n_k) {
         const int64_t gi = wrow * T.n_groups + (T.n_groups > 1 ? ((int64_t)k * kBK) / T.group_size : 0);
         sc = T.scales[gi];
         z = T.zps[gi];
@@ -373,16 +373,16 @@ __global__ void __launch_bounds__(kThreads, 1)
     int s = 0, sb = 0;
     uint32_t ph = 0, phb = 0;
     // one step: wait for the stage's codes and a free B buffer, dequantise, publish
-    auto step = [&](int kt, uint32_t z, float sc) -> bool {
+    auto step = [&](uint32_t z, float sc) -> bool {
       if (!mbar_wait(full + 8 * s, ph, abort_flag)) return false;
       if (!mbar_wait(bempty + 8 * sb, phb ^ 1u, abort_flag)) return false;
-      dequant_row<ACT>(bits, gbase + (w_ring - base) + s * w_tile, r, 8388608.0f + (float)z, sc,
-                       gbase + (b_ring - base) + sb * kBTile + r * 128, live);
+      dequant_half<ACT, BITS>(gbase + (w_ring - base) + s * w_tile, r, h, 8388608.0f + (float)z, sc,
+                              gbase + (b_ring - base) + sb * kBTile + r * 128, live);
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // generic writes -> tensor core
       __syncwarp();
       if (lane == 0) {
         mbar_arrive(empty + 8 * s);   // this warp's raw codes are read
-        mbar_arrive(bfull + 8 * sb);  // and its 32 rows of B written
+        mbar_arrive(bfull + 8 * sb);  // and its 16 rows of B written
       }
       if (++s == n_ls) { s = 0; ph ^= 1u; }
       if (++sb == kBBufs) { sb = 0; phb ^= 1u; }
@@ -396,28 +396,29 @@ __global__ void __launch_bounds__(kThreads, 1)
     load_sz(0, za, sa);
     load_sz(1, zb, sb2);
     for (int kt = 0; kt < n_k; kt += 2) {
-      if (!step(kt, za, sa)) break;
+      if (!step(za, sa)) break;
       load_sz(kt + 2, za, sa);
       if (kt + 1 < n_k) {
-        if (!step(kt + 1, zb, sb2)) break;
+        if (!step(zb, sb2)) break;
         load_sz(kt + 3, zb, sb2);
       }
     }
 
-    // ── epilogue: warp w reads TMEM lanes 32 (w % 4) .. +31 of accumulator (w - 2) / 4 ──
-    // 32 x 32 blocks pass through shared memory (the A ring, idle once every
-    // MMA is done), so that a store instruction writes one token's 32
+    // ── epilogue: warp w reads TMEM lanes 32 (w % 4) .. +31 (the lanes its
+    // rank may access) of accumulator ((w - 2) / 4) % 2, columns 128 ((w - 2) / 8) .. +127 ──
+    // 32 x 32 blocks pass through shared memory (the A and raw rings, idle once
+    // every MMA is done), so that a store instruction writes one token's 32
     // consecutive tier rows (ascending output columns) rather than 32 tokens'
     // rows of one column.
     volatile int never = 0;
     const bool done = mbar_wait(accfull, 0u, &never) && !*abort_flag;
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-    const int q = warp & 3, half = (warp - 2) >> 2;
+    const int q = warp & 3, half = ((warp - 2) >> 2) & 1, c0 = ((warp - 2) >> 3) * 128;
     const int64_t tokw = tok0 + 128 * half + 32 * q;  // this warp's first token
     float* buf = reinterpret_cast<float*>(gbase) + (warp - 2) * (32 * 33);
     if (done && (half == 0 || two) && tokw < M) {
 #pragma unroll 1
-      for (int cb = 0; cb < kBN && row0 + cb < T.n_rows; cb += 32) {
+      for (int cb = c0; cb < c0 + 128 && row0 + cb < T.n_rows; cb += 32) {
         uint32_t v[32];
         const uint32_t taddr = tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)(256 * half + cb);
         asm volatile(
@@ -507,18 +508,26 @@ bool map_codes(CUtensorMap* m, const csaq_tier& t) {
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-template <typename ACT>
-int launch_qgemm(const csaq_tier* tiers, int n_tiers, int64_t K, const void* x, int x_dtype, int64_t M, int64_t ldx,
-                 cudaStream_t st) {
+template <typename ACT, int BITS>
+int launch_tier(const CUtensorMap& mx, const CUtensorMap& mw, const csaq_tier& T, int64_t K, int64_t M,
+                unsigned n_tiles, cudaStream_t st) {
   static std::once_flag once;
   static cudaError_t attr = cudaSuccess;
   std::call_once(once, [] {
-    attr = cudaFuncSetAttribute(qgemm_kernel<ACT>, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxSmem);
+    attr = cudaFuncSetAttribute(qgemm_kernel<ACT, BITS>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                smem_bytes(BITS));
   });
   if (attr != cudaSuccess) {
     set_last_cuda_error(attr);
     return CSAQ_ERR_CUDA;
   }
+  return launch_pdl(qgemm_kernel<ACT, BITS>, dim3(n_tiles), dim3(kThreads), (size_t)smem_bytes(BITS), st, mx, mw, T,
+                    K, M);
+}
+
+template <typename ACT>
+int launch_qgemm(const csaq_tier* tiers, int n_tiers, int64_t K, const void* x, int x_dtype, int64_t M, int64_t ldx,
+                 cudaStream_t st) {
   CUtensorMap mx;
   if (!map_activations(&mx, x, x_dtype, K, M, ldx)) return CSAQ_ERR_UNSUPPORTED;
   for (int i = 0; i < n_tiers; ++i) {
@@ -528,8 +537,11 @@ int launch_qgemm(const csaq_tier* tiers, int n_tiers, int64_t K, const void* x, 
     if (!map_codes(&mw, T)) return CSAQ_ERR_UNSUPPORTED;
     const int64_t n_tiles = ((M + kBM - 1) / kBM) * ((T.n_rows + kBN - 1) / kBN);
     if (n_tiles > INT32_MAX) return CSAQ_ERR_UNSUPPORTED;
-    const int rc = launch_pdl(qgemm_kernel<ACT>, dim3((unsigned)n_tiles), dim3(kThreads),
-                              (size_t)smem_bytes(T.bits), st, mx, mw, T, K, M);
+    const unsigned nt = (unsigned)n_tiles;
+    const int rc = T.bits == 2   ? launch_tier<ACT, 2>(mx, mw, T, K, M, nt, st)
+                   : T.bits == 4 ? launch_tier<ACT, 4>(mx, mw, T, K, M, nt, st)
+                   : T.bits == 8 ? launch_tier<ACT, 8>(mx, mw, T, K, M, nt, st)
+                                 : launch_tier<ACT, 16>(mx, mw, T, K, M, nt, st);
     if (rc) return rc;
   }
   return CSAQ_OK;
