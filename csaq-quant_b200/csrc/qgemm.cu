@@ -38,6 +38,7 @@
 #include <mutex>
 
 #include "common.cuh"
+#include "tile_blocks.cuh"
 
 namespace csaq {
 namespace {
@@ -253,7 +254,7 @@ __device__ __forceinline__ void dequant_half(const uint8_t* tile, int r, int h, 
 template <typename ACT, int BITS>
 __global__ void __launch_bounds__(kThreads, 1)
     qgemm_kernel(const __grid_constant__ CUtensorMap map_x, const __grid_constant__ CUtensorMap map_w,
-                 const csaq_tier T, int64_t K, int64_t M) {
+                 const csaq_tier T, int64_t K, int64_t M, int use_meta) {
   extern __shared__ __align__(16) uint8_t smem_raw[];
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   constexpr int n_ls = load_stages(BITS);
@@ -360,14 +361,31 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int d = tid - 64, r = d >> 1, h = d & 1;
     const int64_t wrow = row0 + r;
     const bool live = wrow < T.n_rows;
+    // Scales and zero points come from the tier's GEMV blocks when it has
+    // them: there a warp's 16 rows have theirs for a 128-column chunk in 80
+    // contiguous bytes (three sectors a load, against sixteen for rows
+    // strided by n_groups in the reference layout).
+    const int rl = lane >> 1;  // row within the warp's 16
+    const uint8_t* meta = nullptr;
+    if (use_meta && BITS != 16 && live) {
+      const int64_t tile16 = wrow / kTileRows;
+      meta = T.blocks + (tile16 / unit_tiles(BITS)) * (K / 128) * chunk_bytes(BITS) +
+             (tile16 % unit_tiles(BITS)) * tile_block_bytes(BITS) + code_bytes(BITS);
+    }
     // scale and zero point of step k (raw: nothing waits on the loads here)
     auto load_sz = [&](int k, uint32_t& z, float& sc) {
       z = 0u;
       sc = 0.0f;
       if (live && BITS != 16 && k < n_k) {
-        const int64_t gi = wrow * T.n_groups + (T.n_groups > 1 ? ((int64_t)k * kBK) / T.group_size : 0);
-        sc = T.scales[gi];
-        z = T.zps[gi];
+        if (meta) {
+          const uint8_t* m = meta + (int64_t)(k >> 1) * chunk_bytes(BITS);
+          sc = reinterpret_cast<const float*>(m)[rl];
+          z = m[64 + rl];
+        } else {
+          const int64_t gi = wrow * T.n_groups + (T.n_groups > 1 ? ((int64_t)k * kBK) / T.group_size : 0);
+          sc = T.scales[gi];
+          z = T.zps[gi];
+        }
       }
     };
     int s = 0, sb = 0;
@@ -511,6 +529,9 @@ bool map_codes(CUtensorMap* m, const csaq_tier& t) {
 template <typename ACT, int BITS>
 int launch_tier(const CUtensorMap& mx, const CUtensorMap& mw, const csaq_tier& T, int64_t K, int64_t M,
                 unsigned n_tiles, cudaStream_t st) {
+  // the GEMV blocks hold one scale per (row, 128 columns): usable when K and
+  // the group size are whole chunks (csaq_repack_tiles accepts nothing else)
+  const int use_meta = T.blocks && K % 128 == 0 && (T.n_groups == 1 || T.group_size % 128 == 0) ? 1 : 0;
   static std::once_flag once;
   static cudaError_t attr = cudaSuccess;
   std::call_once(once, [] {
@@ -522,7 +543,7 @@ int launch_tier(const CUtensorMap& mx, const CUtensorMap& mw, const csaq_tier& T
     return CSAQ_ERR_CUDA;
   }
   return launch_pdl(qgemm_kernel<ACT, BITS>, dim3(n_tiles), dim3(kThreads), (size_t)smem_bytes(BITS), st, mx, mw, T,
-                    K, M);
+                    K, M, use_meta);
 }
 
 template <typename ACT>

@@ -44,13 +44,13 @@
 #include <vector>
 
 #include "common.cuh"
+#include "tile_blocks.cuh"
 
 namespace csaq {
 namespace {
 
 constexpr int kWarps = 16;  // one CTA per SM
 constexpr int kThreads = kWarps * 32;
-constexpr int kTileRows = 16;
 constexpr int kRecStride = 288;  // bytes per (chunk, token) record block: 256 + 32 (bank spread)
 
 struct TierParams {
@@ -87,18 +87,6 @@ __device__ __forceinline__ uint32_t smem_u32(const void* p) {
 }
 __device__ __forceinline__ uint32_t pack_h2(float a, float b) {
   return bits_of<__half>(__float2half_rn(a)) | (bits_of<__half>(__float2half_rn(b)) << 16);
-}
-
-// ── block geometry ──────────────────────────────────────────────────────────
-__host__ __device__ __forceinline__ int unit_tiles(int bits) { return (bits == 2 || bits == 4) ? 2 : 1; }
-__host__ __device__ __forceinline__ int code_bytes(int bits) {  // one tile x one chunk
-  return bits == 2 ? 512 : bits == 4 ? 1024 : bits == 8 ? 2048 : 4096;
-}
-__host__ __device__ __forceinline__ int tile_block_bytes(int bits) {
-  return bits == 16 ? 4096 : (code_bytes(bits) + 80 + 15) / 16 * 16;
-}
-__host__ __device__ __forceinline__ int chunk_bytes(int bits) {  // one unit x one chunk
-  return unit_tiles(bits) * tile_block_bytes(bits);
 }
 
 // ── repack: reference layout -> GEMV blocks ─────────────────────────────────

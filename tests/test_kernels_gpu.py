@@ -366,6 +366,13 @@ def test_qgemm_low_bit_tiers(dtype):
         Wx = torch.from_numpy(Wref).to(dtype).float().numpy()
         tight = 4e-3 if dtype == torch.bfloat16 else 2e-3
         assert_linear_close(got, O.linear_ref(x.float().numpy(), Wx), rtol=tight, what=f"qgemm 8/4/2 x-dtype m={m}")
+        # without the GEMV blocks the scales come from the reference layout: same bits
+        y2 = torch.zeros_like(y)
+        descs = layer.gemv_descriptors(y2)
+        for d in descs:
+            d.blocks = None
+        _lib.qgemm(descs, 1024, x.to(DEV), m)
+        assert torch.equal(y2, y)
 
 
 def test_qgemm_token_result_independent_of_m():
