@@ -14,7 +14,8 @@
 //     "high" positions times 16, exact).
 //   * Work = (unit, chunk) items of every tier of the launch, spread over the
 //     warps of a one-CTA-per-SM grid of 2-CTA clusters: each cluster takes a
-//     run of whole units, cut so the clusters carry equal block bytes, and
+//     run of whole units, cut so the clusters carry equal cost (measured time
+//     per item by bit-width), and
 //     each of its 32 warps an equal-cost run of items (stream-K). Each warp
 //     streams its blocks into a shared-memory ring by bulk copies. A unit
 //     whose chunks all fall in one warp's range is finished in registers; a
@@ -324,16 +325,6 @@ __device__ __forceinline__ int tier_of_item(const KParams& P, int item) {
   return t;
 }
 
-// the warp whose (non-empty) range holds `item`: the largest w with begin[w] <= item
-__device__ __forceinline__ int warp_of_item(const KParams& P, int item) {
-  int lo = 0, hi = P.n_warps - 1;
-  while (lo < hi) {
-    const int mid = (lo + hi + 1) >> 1;
-    if (P.begin[mid] <= item) lo = mid; else hi = mid - 1;
-  }
-  return lo;
-}
-
 template <typename ACT>
 __device__ __forceinline__ void store_out(const csaq_tier& T, int row, int tok, float v, float xe) {
   v = __fmul_rn(v, xe);
@@ -393,9 +384,12 @@ __device__ __forceinline__ uint32_t dsmem_addr(uint32_t saddr, int rank) {
   asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(saddr), "r"(rank));
   return r;
 }
-__device__ __forceinline__ float ld_dsmem_f32(uint32_t addr) {
+// A load of data that no thread writes any more (after a cluster barrier):
+// not volatile, so that independent loads are issued back to back. It stays
+// after the barrier because its address comes from mapa, which is volatile.
+__device__ __forceinline__ float ld_dsmem_f32_after_sync(uint32_t addr) {
   float v;
-  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(addr) : "memory");
+  asm("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(addr));
   return v;
 }
 
@@ -581,17 +575,20 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kThreads, 1)
   if (threadIdx.x < 16) smax[threadIdx.x] = 0u;
   __syncthreads();
   const int k8 = (int)(K / 8);
-  for (int tok = 0; tok < M; ++tok) {
-    float mx = 0.0f;
-    for (int kk = threadIdx.x; kk < k8; kk += blockDim.x) {
-      const uint4 q = ld_cached_v4(x + (int64_t)tok * ldx + 8 * kk);
-      const ACT* e = reinterpret_cast<const ACT*>(&q);
+  {  // the tokens side by side: warp w scans part w / M of token w % M (M <= kWarps)
+    const int wpt = kWarps / M, tok = warp % M, part = warp / M;
+    if (part < wpt) {
+      float mx = 0.0f;
+      for (int kk = part * 32 + lane; kk < k8; kk += wpt * 32) {
+        const uint4 q = ld_cached_v4(x + (int64_t)tok * ldx + 8 * kk);
+        const ACT* e = reinterpret_cast<const ACT*>(&q);
 #pragma unroll
-      for (int j = 0; j < 8; ++j) mx = fmaxf(mx, fabsf(to_f32<ACT>(e[j])));
+        for (int j = 0; j < 8; ++j) mx = fmaxf(mx, fabsf(to_f32<ACT>(e[j])));
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+      if (lane == 0 && mx > 0.0f) atomicMax(&smax[tok], __float_as_uint(mx));
     }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-    if (lane == 0 && mx > 0.0f) atomicMax(&smax[tok], __float_as_uint(mx));
   }
   __syncthreads();
   if (threadIdx.x < 16) {
@@ -737,6 +734,16 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kThreads, 1)
   cluster_sync();  // partials of both CTAs written and visible
 
   const uint32_t part_sa = smem_u32(part);
+  // the range starts of this cluster's 32 warps, lane l holding warp
+  // cl_base + l's (kernel-parameter loads with a varying index are slow):
+  // begin[w] of any warp of the cluster is one shuffle away
+  static_assert(kWarps * kCluster == 32, "one lane per warp of a cluster");
+  const int cl_base = wg - (wg & 31);
+  const int b_lane = P.begin[cl_base + lane], b_end = P.begin[cl_base + 32];
+  auto begin_of = [&](int w) {  // w in [cl_base, cl_base + 32]
+    const int v = __shfl_sync(0xffffffffu, b_lane, (w - cl_base) & 31);
+    return w - cl_base == 32 ? b_end : v;
+  };
 #pragma unroll 1
   for (int s = 0; s < 2; ++s) {
     const int ut = s == 0 ? cut_t0 : cut_t1;
@@ -745,7 +752,7 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kThreads, 1)
     const int u_start = s == 0 ? cut_s0 : cut_s1, u_end = u_start + n_chunks;
     // units never cross a cluster boundary; the highest warp holding part of
     // the unit adds the partials in warp order and writes y
-    if (P.begin[wg + 1] < u_end) continue;
+    if (begin_of(wg + 1) < u_end) continue;
     const TierWork& tw = P.w[ut];
     const csaq_tier& T = P.tp.t[ut];
     const int rows = tw.mt * kTileRows;
@@ -753,16 +760,32 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kThreads, 1)
     float v[16];
 #pragma unroll
     for (int j = 0; j < 16; ++j) v[j] = 0.0f;
-    for (int w = warp_of_item(P, u_start); w <= wg; ++w) {
-      const int b = P.begin[w];
-      if (b == P.begin[w + 1]) continue;  // empty range
-      const uint32_t off = (uint32_t)((((w % kWarps) * 2 + (b >= u_start ? 0 : 1)) * 32 * M) * 4);
-      const uint32_t src = dsmem_addr(part_sa + off, (w / kWarps) % kCluster);
+    // eight warps' partials at a time: their loads are issued together and
+    // added in warp order afterwards
+    // first warp holding part of the unit: the last of the cluster with begin <= u_start
+    const int w_first = cl_base + 31 - __clz(__ballot_sync(0xffffffffu, b_lane <= u_start));
+    for (int w0 = w_first; w0 <= wg; w0 += 8) {
+      uint32_t src[8];
+      bool ok[8];
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {
+        const int w = w0 + q;
+        const int bw = begin_of(w <= wg ? w : wg), bw1 = begin_of(w <= wg ? w + 1 : wg + 1);
+        ok[q] = w <= wg && bw != bw1;  // skip empty ranges
+        const uint32_t off = ok[q] ? (uint32_t)((((w % kWarps) * 2 + (bw >= u_start ? 0 : 1)) * 32 * M) * 4) : 0u;
+        src[q] = ok[q] ? dsmem_addr(part_sa + off, (w / kWarps) % kCluster) : 0u;
+      }
 #pragma unroll
       for (int j = 0; j < 16; ++j) {
         if (j >= nv) break;
         const int e = lane + 32 * j;
-        if (e < n_val) v[j] += ld_dsmem_f32(src + 4u * (uint32_t)e);
+        if (e >= n_val) continue;
+        float a[8];
+#pragma unroll
+        for (int q = 0; q < 8; ++q) a[q] = ok[q] ? ld_dsmem_f32_after_sync(src[q] + 4u * (uint32_t)e) : 0.0f;
+#pragma unroll
+        for (int q = 0; q < 8; ++q)
+          if (ok[q]) v[j] += a[q];
       }
     }
 #pragma unroll
@@ -916,7 +939,7 @@ int64_t work_table(const TierParams& TP, int64_t K, TierWork* w) {
 // between two unit boundaries, chosen nearest to the cost targets C j / G, so
 // that no unit leaves its cluster; inside a cluster its kCluster * kWarps
 // warps take runs of equal cost, cut at chunk granularity (item start cost >=
-// the warp's target). Costs are block bytes / 16.
+// the warp's target). Costs are item_cost() per item.
 struct PartitionCache {
   struct Entry {
     std::vector<int> key;
@@ -926,6 +949,13 @@ struct PartitionCache {
   std::vector<Entry> entries;
   size_t next = 0;
 };
+
+// Relative time of one item (a unit's 128-column chunk) by bit-width, as
+// measured on B200 with every warp streaming: a 16-bit item (16 rows, 4 KB)
+// takes about 0.8 of a 4-bit item (32 rows, 2.2 KB), an 8-bit one (16 rows as
+// two nibble planes) about as long as a 4-bit one. Warps streaming fp16 rows
+// finish early when items are costed by bytes.
+int64_t item_cost(int bits) { return bits == 16 ? 82 : (bits == 8 ? 100 : 100); }
 
 bool partition(const TierParams& TP, const TierWork* w, int64_t K, int n_warps, int* begin) {
   static PartitionCache cache;
@@ -949,7 +979,7 @@ bool partition(const TierParams& TP, const TierWork* w, int64_t K, int n_warps, 
   std::vector<int64_t> ic(n_tiers), cost0(n_tiers + 1);
   cost0[0] = 0;
   for (int i = 0; i < n_tiers; ++i) {
-    ic[i] = chunk_bytes(w[i].bits) / 16;
+    ic[i] = item_cost(w[i].bits);
     cost0[i + 1] = cost0[i] + ic[i] * w[i].n_items;
   }
   const int64_t total = cost0[n_tiers];
