@@ -198,22 +198,32 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attention_kernel(
     const T* __restrict__ q, const T* __restrict__ k_cache, const T* __restrict__ v_cache,
     const int32_t* __restrict__ pos0, int S, int Hq, int Hkv, int Lmax, float scale,
     float* __restrict__ part, int32_t* __restrict__ tickets, T* __restrict__ out) {
-  pdl_wait();
-  pdl_trigger();
   constexpr int D = 128;
   const int bh = blockIdx.x, sp = blockIdx.y, n_split = gridDim.y;
   const int b = bh / Hkv, h = bh % Hkv;
   const int G = Hq / Hkv, R = S * G;
-  const int len = pos0[b] + S;  // keys visible to the last new token
+  // pos0 and the cache below pos0 were written steps ago, by kernels that
+  // finished before the one this launch may overlap (which waits for its own
+  // predecessor before it lets this one start): the chunk's old keys and
+  // values are copied before waiting, the new ones (written by the
+  // predecessor) after
+  const int p0 = pos0[b];
+  const int len = p0 + S;  // keys visible to the last new token
   const int k0 = sp * kChunk;
   __shared__ __align__(16) T ks[kChunk][D];
   __shared__ __align__(16) T vs[kChunk][D];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int n_keys = max(0, min(kChunk, len - k0));
+  const int n_old = max(0, min(n_keys, p0 - k0));
   const T* kb = k_cache + (((int64_t)b * Hkv + h) * Lmax + k0) * D;
   const T* vb = v_cache + (((int64_t)b * Hkv + h) * Lmax + k0) * D;
-  // the chunk's keys and values: one wave of 16-byte asynchronous copies
-  for (int e = threadIdx.x; e < n_keys * D / 8; e += blockDim.x) {
+  for (int e = threadIdx.x; e < n_old * D / 8; e += blockDim.x) {
+    cp_async16(reinterpret_cast<uint4*>(&ks[0][0]) + e, reinterpret_cast<const uint4*>(kb) + e);
+    cp_async16(reinterpret_cast<uint4*>(&vs[0][0]) + e, reinterpret_cast<const uint4*>(vb) + e);
+  }
+  pdl_wait();
+  pdl_trigger();
+  for (int e = n_old * D / 8 + threadIdx.x; e < n_keys * D / 8; e += blockDim.x) {
     cp_async16(reinterpret_cast<uint4*>(&ks[0][0]) + e, reinterpret_cast<const uint4*>(kb) + e);
     cp_async16(reinterpret_cast<uint4*>(&vs[0][0]) + e, reinterpret_cast<const uint4*>(vb) + e);
   }
@@ -355,13 +365,35 @@ __global__ void __launch_bounds__(kArgThreads) argmax_kernel(const T* __restrict
   const int64_t m = blockIdx.x;
   float best = -INFINITY;
   int64_t bi = INT64_MAX;
+  auto take = [&](float v, int64_t g) {
+    if (v > best || (v == best && g < bi)) { best = v; bi = g; }
+  };
   for (int r = 0; r < n_parts; ++r) {
     const T* row = logits + r * part_stride + m * ld;
-    for (int64_t j = threadIdx.x; j < part_len; j += blockDim.x) {
-      const float v = to_f32<T>(row[j]);
-      const int64_t g = r * part_len + j;
-      if (v > best || (v == best && g < bi)) { best = v; bi = g; }
+    int64_t j0 = 0;
+    if (reinterpret_cast<uintptr_t>(row) % 16 == 0) {
+      // 8 values per 16-byte load, four loads in flight per thread
+      const int64_t n8 = part_len / 8;
+      const uint4* rv = reinterpret_cast<const uint4*>(row);
+      for (int64_t j = threadIdx.x; j < n8; j += 4 * (int64_t)blockDim.x) {
+        uint4 q[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const int64_t jj = j + u * (int64_t)blockDim.x;
+          q[u] = jj < n8 ? __ldcs(rv + jj) : make_uint4(0u, 0u, 0u, 0u);
+        }
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const int64_t jj = j + u * (int64_t)blockDim.x;
+          if (jj >= n8) break;
+          const T* e = reinterpret_cast<const T*>(&q[u]);
+#pragma unroll
+          for (int t = 0; t < 8; ++t) take(to_f32<T>(e[t]), r * part_len + 8 * jj + t);
+        }
+      }
+      j0 = n8 * 8;
     }
+    for (int64_t j = j0 + threadIdx.x; j < part_len; j += blockDim.x) take(to_f32<T>(row[j]), r * part_len + j);
   }
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) {
