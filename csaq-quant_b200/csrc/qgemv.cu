@@ -315,7 +315,9 @@ struct KParams {
   int slot_bytes;  // ring slot: the largest chunk_bytes of the launch
   int depth;       // ring slots per warp
   int want2;       // any 2-bit tier (stage R2 records)
-  int x_bytes;     // R4 records: n_chunks * M * kRecStride (R2 the same again when want2)
+  int x_bytes;     // R4 records: n_rec * M * kRecStride (R2 the same again when want2)
+  int split;       // records split by chunk between the cluster's CTAs (they do not fit one)
+  int ch_half;     // split: CTA rank 0 holds chunks [0, ch_half), rank 1 the rest
   int begin[kMaxWarps + 1];
 };
 
@@ -395,10 +397,13 @@ __device__ __forceinline__ float ld_dsmem_f32_after_sync(uint32_t addr) {
 
 // One 128-column chunk of one unit: acc[tile][n-tile][fragment] += the chunk's
 // contribution (see the header comment for the algebra).
-template <int BITS, int NT>
+// DS: the chunk's records and (C, S) live in the other CTA of the cluster
+// (or this one) and are read through distributed shared memory at the
+// shared::cluster addresses rb_cl and xcs_cl; otherwise at rbase and xcs_ch.
+template <int BITS, int NT, bool DS>
 __device__ __forceinline__ void chunk_math(const uint8_t* slot, const uint8_t* rbase,
-                                           const float4* xcs_ch, int M, int lane,
-                                           float (&acc)[2][NT][4]) {
+                                           const float4* xcs_ch, uint32_t rb_cl, uint32_t xcs_cl, int M,
+                                           int lane, float (&acc)[2][NT][4]) {
   constexpr int bits = BITS;
   const int g = lane >> 2, c = lane & 3;
 #pragma unroll
@@ -406,16 +411,37 @@ __device__ __forceinline__ void chunk_math(const uint8_t* slot, const uint8_t* r
     const int tok = nt * 8 + g;
     uint2 rec[8];
     if (tok < M) {
-      const uint2* rp = reinterpret_cast<const uint2*>(rbase + tok * kRecStride) + c;
+      if constexpr (DS) {
+        const uint32_t ra = rb_cl + (uint32_t)(tok * kRecStride + 8 * c);
 #pragma unroll
-      for (int q = 0; q < 8; ++q) rec[q] = rp[4 * q];
+        for (int q = 0; q < 8; ++q)
+          asm volatile("ld.shared::cluster.v2.u32 {%0, %1}, [%2];"
+                       : "=r"(rec[q].x), "=r"(rec[q].y)
+                       : "r"(ra + 32u * q));
+      } else {
+        const uint2* rp = reinterpret_cast<const uint2*>(rbase + tok * kRecStride) + c;
+#pragma unroll
+        for (int q = 0; q < 8; ++q) rec[q] = rp[4 * q];
+      }
     } else {
 #pragma unroll
       for (int q = 0; q < 8; ++q) rec[q] = make_uint2(0u, 0u);
     }
     const int t0 = nt * 8 + 2 * c;
-    const float4 cs0 = t0 < M ? xcs_ch[t0] : make_float4(0.f, 0.f, 0.f, 0.f);
-    const float4 cs1 = t0 + 1 < M ? xcs_ch[t0 + 1] : make_float4(0.f, 0.f, 0.f, 0.f);
+    float4 cs0 = make_float4(0.f, 0.f, 0.f, 0.f), cs1 = make_float4(0.f, 0.f, 0.f, 0.f);
+    if constexpr (DS) {
+      if (t0 < M)
+        asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];"
+                     : "=f"(cs0.x), "=f"(cs0.y), "=f"(cs0.z), "=f"(cs0.w)
+                     : "r"(xcs_cl + 16u * t0));
+      if (t0 + 1 < M)
+        asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];"
+                     : "=f"(cs1.x), "=f"(cs1.y), "=f"(cs1.z), "=f"(cs1.w)
+                     : "r"(xcs_cl + 16u * (t0 + 1)));
+    } else {
+      if (t0 < M) cs0 = xcs_ch[t0];
+      if (t0 + 1 < M) cs1 = xcs_ch[t0 + 1];
+    }
     if constexpr (bits == 4 || bits == 8) {
       // 4-bit: [tile][h][word]; 8-bit: [nibble plane][h][word] of one tile
       uint32_t cw[2][2][4];
@@ -516,7 +542,7 @@ struct UnitRef {
   int t, unit, start, end;  // items [start, end)
 };
 
-template <typename ACT, int NT>
+template <typename ACT, int NT, bool SPLIT>
 __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kThreads, 1)
     qgemv_mma_kernel(const __grid_constant__ KParams P,
                                                                 int64_t K, const ACT* __restrict__ x,
@@ -528,7 +554,8 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kThreads, 1)
   uint8_t* rec4 = smem;                                          // [ch][tok] x kRecStride
   uint8_t* rec2 = smem + P.x_bytes;                              // same layout, 2-bit records
   float4* xcs = reinterpret_cast<float4*>(smem + (P.want2 ? 2 : 1) * P.x_bytes);  // [ch][tok] (C4, S, C2, -)
-  float* xexp = reinterpret_cast<float*>(xcs + n_chunks * M);    // [16] 2^e per token
+  const int n_rec = SPLIT ? P.ch_half : n_chunks;                // chunks of records held here
+  float* xexp = reinterpret_cast<float*>(xcs + n_rec * M);       // [16] 2^e per token
   uint64_t* bars = reinterpret_cast<uint64_t*>(xexp + 16) + warp * 8;  // [warp][8] ring barriers
   uint8_t* ring_all = reinterpret_cast<uint8_t*>(xexp + 16) + kWarps * 8 * sizeof(uint64_t);
   uint8_t* ring = ring_all + (size_t)warp * P.depth * P.slot_bytes;
@@ -598,13 +625,17 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kThreads, 1)
   }
   __syncthreads();
 
-  // activation records (whole warps iterate: 4-lane shuffles)
-  const int n_st = M * n_chunks * 4;
+  // activation records (whole warps iterate: 4-lane shuffles); split: this
+  // CTA builds and holds the records of its own chunk half only
+  const int rank = (int)(blockIdx.x % kCluster);
+  const int c_lo = SPLIT ? rank * P.ch_half : 0;
+  const int n_loc = SPLIT ? (rank == 0 ? P.ch_half : n_chunks - P.ch_half) : n_chunks;
+  const int n_st = M * n_loc * 4;
   for (int base = 0; base < n_st; base += blockDim.x) {
     const int u = base + threadIdx.x;
     const bool live = u < n_st;
     const int cc = u & 3, rest = u >> 2;
-    const int tok = live ? rest % M : 0, ch = live ? rest / M : 0;
+    const int tok = live ? rest % M : 0, li = live ? rest / M : 0, ch = c_lo + li;
     uint2 r4[8], r2[8];
     float C4 = 0.0f, C2 = 0.0f, S = 0.0f;
     if (live) build_records<ACT>(x + (int64_t)tok * ldx + ch * 128 + cc * 32, 1.0f / xexp[tok],
@@ -616,18 +647,21 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kThreads, 1)
       S += __shfl_xor_sync(0xffffffffu, S, o);
     }
     if (live) {
-      uint2* d4 = reinterpret_cast<uint2*>(rec4 + ((int64_t)ch * M + tok) * kRecStride) + cc;
+      uint2* d4 = reinterpret_cast<uint2*>(rec4 + ((int64_t)li * M + tok) * kRecStride) + cc;
 #pragma unroll
       for (int j = 0; j < 8; ++j) d4[4 * j] = r4[j];
       if (P.want2) {
-        uint2* d2 = reinterpret_cast<uint2*>(rec2 + ((int64_t)ch * M + tok) * kRecStride) + cc;
+        uint2* d2 = reinterpret_cast<uint2*>(rec2 + ((int64_t)li * M + tok) * kRecStride) + cc;
 #pragma unroll
         for (int j = 0; j < 8; ++j) d2[4 * j] = r2[j];
       }
-      if (cc == 0) xcs[ch * M + tok] = make_float4(C4, S, C2, 0.0f);
+      if (cc == 0) xcs[li * M + tok] = make_float4(C4, S, C2, 0.0f);
     }
   }
-  __syncthreads();
+  if constexpr (SPLIT)
+    cluster_sync();  // both halves of the records are written and visible
+  else
+    __syncthreads();
 
   // ── main loop over the warp's units ──────────────────────────────────────
   float acc[2][NT][4], fst[2][NT][4];
@@ -649,8 +683,15 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kThreads, 1)
         late_parity = (late_parity & ~(1u << c_slot)) | (phase & (1u << c_slot));
       }
       phase ^= 1u << c_slot;
-      chunk_math<B, NT>(ring + c_slot * P.slot_bytes, (B == 2 ? rec2 : rec4) + (int64_t)ch * M * kRecStride,
-                        xcs + ch * M, M, lane, acc);
+      if constexpr (SPLIT) {
+        const int r = ch >= P.ch_half ? 1 : 0, li = ch - r * P.ch_half;
+        const uint32_t rb = dsmem_addr(smem_u32((B == 2 ? rec2 : rec4) + (int64_t)li * M * kRecStride), r);
+        const uint32_t xb = dsmem_addr(smem_u32(xcs + li * M), r);
+        chunk_math<B, NT, true>(ring + c_slot * P.slot_bytes, nullptr, nullptr, rb, xb, M, lane, acc);
+      } else {
+        chunk_math<B, NT, false>(ring + c_slot * P.slot_bytes, (B == 2 ? rec2 : rec4) + (int64_t)ch * M * kRecStride,
+                                 xcs + ch * M, 0u, 0u, M, lane, acc);
+      }
       __syncwarp();
       issue();
       c_slot = (c_slot + 1 == P.depth) ? 0 : c_slot + 1;
@@ -1032,7 +1073,7 @@ bool partition(const TierParams& TP, const TierWork* w, int64_t K, int n_warps, 
 }
 
 struct Plan {
-  int x_bytes, smem_bytes, depth, slot_bytes, want2;
+  int x_bytes, smem_bytes, depth, slot_bytes, want2, split, ch_half;
 };
 
 bool make_plan(const TierParams& TP, int64_t K, int M, Plan& p) {
@@ -1046,24 +1087,32 @@ bool make_plan(const TierParams& TP, int64_t K, int M, Plan& p) {
     if (TP.t[i].bits == 2) p.want2 = 1;
   }
   if (p.slot_bytes == 0) p.slot_bytes = 16;
-  p.x_bytes = n_chunks * M * kRecStride;
-  // records, (C, S) per chunk and token, 2^e per token, ring barriers
-  const int fixed = (p.want2 ? 2 : 1) * p.x_bytes + n_chunks * M * 16 + 64 + kWarps * 8 * 8;
   const int part_bytes = kWarps * 2 * 32 * M * 4;  // reuses the rings after the main loop
-  int depth = kRingBudget / p.slot_bytes;
-  depth = depth < 2 ? 2 : (depth > 8 ? 8 : depth);
   auto ring_bytes = [&](int d) { return kWarps * d * p.slot_bytes > part_bytes ? kWarps * d * p.slot_bytes : part_bytes; };
-  while (depth > 2 && fixed + ring_bytes(depth) > kSmemBudget) --depth;
-  p.depth = depth;
-  p.smem_bytes = fixed + ring_bytes(depth);
-  return p.smem_bytes <= kSmemBudget;
+  // whole records first; when they do not fit beside a 2-deep ring, each CTA
+  // of a cluster holds half of the chunks and reads the other half from its peer
+  for (int split = 0; split < 2; ++split) {
+    p.split = split;
+    p.ch_half = split ? (n_chunks + 1) / 2 : n_chunks;
+    const int n_rec = p.ch_half;
+    p.x_bytes = n_rec * M * kRecStride;
+    // records, (C, S) per chunk and token, 2^e per token, ring barriers
+    const int fixed = (p.want2 ? 2 : 1) * p.x_bytes + n_rec * M * 16 + 64 + kWarps * 8 * 8;
+    int depth = kRingBudget / p.slot_bytes;
+    depth = depth < 2 ? 2 : (depth > 8 ? 8 : depth);
+    while (depth > 2 && fixed + ring_bytes(depth) > kSmemBudget) --depth;
+    p.depth = depth;
+    p.smem_bytes = fixed + ring_bytes(depth);
+    if (p.smem_bytes <= kSmemBudget) return true;
+  }
+  return false;
 }
 
-template <typename ACT, int NT>
+template <typename ACT, int NT, bool SPLIT>
 int set_smem_attr() {
   static bool done = false;
   if (!done) {
-    if (cudaFuncSetAttribute(qgemv_mma_kernel<ACT, NT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    if (cudaFuncSetAttribute(qgemv_mma_kernel<ACT, NT, SPLIT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              kSmemBudget) != cudaSuccess)
       return launch_status();
     done = true;
@@ -1075,7 +1124,7 @@ template <typename ACT, int NT>
 int launch_mma_block(const TierParams& TP, int64_t K, const ACT* x, int M, int64_t ldx, cudaStream_t st) {
   Plan pl;
   if (!make_plan(TP, K, M, pl)) return CSAQ_ERR_UNSUPPORTED;
-  int rc = set_smem_attr<ACT, NT>();
+  int rc = pl.split ? set_smem_attr<ACT, NT, true>() : set_smem_attr<ACT, NT, false>();
   if (rc) return rc;
   static thread_local KParams P;  // about 12 KB: kept off the stack
   P.tp = TP;
@@ -1087,13 +1136,18 @@ int launch_mma_block(const TierParams& TP, int64_t K, const ACT* x, int M, int64
   P.depth = pl.depth;
   P.want2 = pl.want2;
   P.x_bytes = pl.x_bytes;
+  P.split = pl.split;
+  P.ch_half = pl.ch_half;
   // the grid depends on the shapes and the SM count only (never on M)
   int ctas = (items + kWarps - 1) / kWarps;
   ctas = (ctas + kCluster - 1) / kCluster * kCluster;
   ctas = ctas < grid_ctas_max() ? ctas : grid_ctas_max();
   P.n_warps = ctas * kWarps;
   partition(TP, P.w, K, P.n_warps, P.begin);
-  return launch_pdl(qgemv_mma_kernel<ACT, NT>, dim3((unsigned)ctas), dim3(kThreads), (size_t)pl.smem_bytes, st,
+  if (pl.split)
+    return launch_pdl(qgemv_mma_kernel<ACT, NT, true>, dim3((unsigned)ctas), dim3(kThreads), (size_t)pl.smem_bytes,
+                      st, P, K, x, M, ldx);
+  return launch_pdl(qgemv_mma_kernel<ACT, NT, false>, dim3((unsigned)ctas), dim3(kThreads), (size_t)pl.smem_bytes, st,
                     P, K, x, M, ldx);
 }
 

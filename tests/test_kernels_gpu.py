@@ -205,6 +205,22 @@ def test_qgemv_mixed_matches_oracle(dtype, m):
     assert_linear_close(y, y_ref, what=f"{dtype} m={m}")
 
 
+@pytest.mark.parametrize("m", [5, 8])
+def test_qgemv_long_k_split_records_matches_oracle(m):
+    """K = 14336 with several tokens: the activation records no longer fit one
+    CTA, so the two CTAs of a cluster each hold half of the chunks (read by
+    the other through distributed shared memory). Against the oracle, and
+    bitwise equal to one token at a time."""
+    layer, case, _ = _mixed_layer(300, 14336, seed=m, dtype=torch.bfloat16, bias=True)
+    Wref = _oracle_mixed(case)
+    x = torch.randn(m, 14336, generator=torch.Generator().manual_seed(m)).to(torch.bfloat16)
+    y = layer(x.to(DEV))
+    y_ref = O.linear_ref(x.float().numpy(), Wref, layer.bias.float().cpu().numpy())
+    assert_linear_close(y.float().cpu().numpy(), y_ref, what=f"K=14336 m={m}")
+    y1 = torch.cat([layer(x[i:i + 1].to(DEV)) for i in range(m)])
+    assert torch.equal(y1, y)
+
+
 @pytest.mark.parametrize("bits", [(2,), (4,), (8,), (16,), (8, 2), (16, 4, 2)])
 @pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
 def test_qgemv_every_bit_width(bits, dtype):
