@@ -34,15 +34,18 @@ from typing import Dict, List, Optional
 
 import torch
 import torch.nn as nn
+import torch.nn.functional as F
 
 from . import _lib
 from ._lib import check, dtype_code, lib, ptr
 from .kernels import CSAQLinear
 
 # Prefill chunks of at least this many tokens use the tcgen05 GEMM; smaller
-# steps (decode, verify, the default 64-token prefill chunks) use the GEMV,
-# which is faster there.
+# steps (decode, verify, short prompts) use the GEMV, which is faster there.
 RUNTIME_GEMM_MIN_TOKENS = 256
+# Prefill chunks of at least this many tokens use torch's fused attention
+# (the decode attention kernel splits keys, not queries, and suits few rows).
+PREFILL_SDPA_TOKENS = 32
 
 
 def _layers_of(model: nn.Module):
@@ -93,7 +96,7 @@ class DecodeRuntime:
     """Decode / self-speculative generation for a quantised Llama/Qwen2 model."""
 
     def __init__(self, model: nn.Module, max_batch: int, max_len: int, lookahead: int = 4,
-                 prefill_chunk: int = 64, tp_group=None):
+                 prefill_chunk: int = 512, tp_group=None):
         if not supports(model):
             raise ValueError("model is not a Llama/Qwen2 decoder with CSAQLinear layers")
         import torch.distributed as dist
@@ -243,13 +246,41 @@ class DecodeRuntime:
         check(lib().csaq_rank_sum(sh.y_all.data_ptr(), self.tp, sh.y_all.stride(0), H, sh.x.data_ptr(), H, M, H, 1,
                                   self.dt, st), "rank_sum")
 
+    def _attention(self, li: int, sh: "_Shape", S: int, pos: torch.Tensor, pos_host: Optional[int],
+                   scale: float, st: int) -> None:
+        """Attention of the step's queries over the cache. Prefill chunks of
+        PREFILL_SDPA_TOKENS tokens or more (all sequences at the same host-known
+        start) go to torch's fused scaled-dot-product attention; decode and
+        verify steps to the split-key decode kernel."""
+        if pos_host is not None and S >= PREFILL_SDPA_TOKENS:
+            B, Hq, Hkv, D = self.B, self.Hq_l, self.Hkv_l, self.D
+            n = pos_host + S
+            q = sh.q_rot.view(B, S, Hq, D).transpose(1, 2)
+            k = self.k_cache[li][:, :, :n]
+            v = self.v_cache[li][:, :, :n]
+            if pos_host == 0:
+                o = F.scaled_dot_product_attention(q, k, v, is_causal=True, scale=scale, enable_gqa=Hq != Hkv)
+            else:  # query i sits at position pos_host + i
+                qi = torch.arange(S, device=self.dev).unsqueeze(1) + pos_host
+                mask = torch.arange(n, device=self.dev).unsqueeze(0) <= qi
+                o = F.scaled_dot_product_attention(q, k, v, attn_mask=mask, scale=scale, enable_gqa=Hq != Hkv)
+            sh.attn.view(B, S, Hq, D).copy_(o.transpose(1, 2))
+            return
+        check(lib().csaq_decode_attention(sh.q_rot.data_ptr(), self.k_cache[li].data_ptr(),
+                                          self.v_cache[li].data_ptr(), pos.data_ptr(), self.B, S, self.Hq_l,
+                                          self.Hkv_l, self.D, self.Lmax, scale, sh.part.data_ptr(),
+                                          self.tickets[li].data_ptr(), sh.attn.data_ptr(), self.dt, st),
+              "attention")
+
     @torch.no_grad()
     def step(self, S: int, ids: torch.Tensor, pos: torch.Tensor, verify: bool,
-             last_only: bool = False) -> torch.Tensor:
+             last_only: bool = False, pos_host: Optional[int] = None) -> torch.Tensor:
         """Run all layers for B*S tokens (ids: B*S int64, pos: per-sequence
-        start positions) and leave the logits of this rank's vocabulary slice
-        in the shape's logits buffer (M rows, or the B rows of the last token
-        of each sequence when last_only); returns the number of logit rows."""
+        start positions; pos_host: the same start for every sequence, when the
+        host knows it, as in prefill) and leave the logits of this rank's
+        vocabulary slice in the shape's logits buffer (M rows, or the B rows of
+        the last token of each sequence when last_only); returns the number of
+        logit rows."""
         sh = self._shape(S)
         L = lib()
         st = torch.cuda.current_stream(self.dev).cuda_stream
@@ -267,11 +298,7 @@ class DecodeRuntime:
                                  Hq, Hkv, D, self.cos.data_ptr(), self.sin.data_ptr(),
                                  sh.q_rot.data_ptr(), self.k_cache[li].data_ptr(),
                                  self.v_cache[li].data_ptr(), self.Lmax, self.dt, st), "rope_kv")
-            check(L.csaq_decode_attention(sh.q_rot.data_ptr(), self.k_cache[li].data_ptr(),
-                                          self.v_cache[li].data_ptr(), pos.data_ptr(), self.B, S, Hq,
-                                          Hkv, D, self.Lmax, scale, sh.part.data_ptr(),
-                                          self.tickets[li].data_ptr(), sh.attn.data_ptr(), self.dt,
-                                          st), "attention")
+            self._attention(li, sh, S, pos, pos_host, scale, st)
             self._gemv(sh.descs[(li, "o", verify)], nq, sh.attn, M, st)
             if self.tp > 1:
                 self._combine(sh, M, st)
@@ -349,7 +376,7 @@ class DecodeRuntime:
             chunk = prompts[:, s0:s0 + C]
             S = chunk.shape[1]
             self.pos0.fill_(s0)
-            self.step(S, chunk.contiguous().view(-1), self.pos0, verify=verify, last_only=True)
+            self.step(S, chunk.contiguous().view(-1), self.pos0, verify=verify, last_only=True, pos_host=s0)
         self.prefill_logits = self.logits_full(S, self.B)
         self.argmax(S, self.B, self.next_tok)
         self.out_tokens[:, 0] = self.next_tok

@@ -49,19 +49,27 @@ def test_runtime_logits_match_hf(which, verify, request):
     from csaq.inference import CSAQInferenceEngine
     model, cmap, _ = request.getfixturevalue(which)
     V = model.config.vocab_size
-    prompt = _prompt(1, 70, V, seed=3)  # two prefill chunks (64 + 6)
+    prompt = _prompt(1, 70, V, seed=3)
     eng = CSAQInferenceEngine(model, cmap, verbose=False)
     rt = eng.runtime(1, 256, 4)
-    rt.reset(prompt.to(DEV), max_new=4, verify=verify)
+    rt.reset(prompt.to(DEV), max_new=4, verify=verify)  # one prefill chunk (fused attention)
     got = rt.prefill_logits.float()
+    rt.prefill_chunk = 32
+    rt.reset(prompt.to(DEV), max_new=4, verify=verify)  # 32 + 32 (fused attention, causal / offset mask) + 6
+    got2 = rt.prefill_logits.float()
+    rt.prefill_chunk = 16
+    rt.reset(prompt.to(DEV), max_new=4, verify=verify)  # 16-token chunks: decode attention kernel
+    got3 = rt.prefill_logits.float()
+    rt.prefill_chunk = 512
     (eng._swap_to_verify if verify else eng._swap_to_draft)()
     with torch.no_grad():
         ref = model(prompt.to(DEV)).logits[:, -1].float()
     eng._swap_to_draft()
-    err = (got - ref).abs().max().item() / ref.abs().max().item()
-    assert err < 3e-2, err
-    cos = torch.nn.functional.cosine_similarity(got, ref).item()
-    assert cos > 0.999, cos
+    for g in (got, got2, got3):
+        err = (g - ref).abs().max().item() / ref.abs().max().item()
+        assert err < 3e-2, err
+        cos = torch.nn.functional.cosine_similarity(g, ref).item()
+        assert cos > 0.999, cos
 
 
 def test_verify_weights_differ_from_draft(tiny_llama):
