@@ -49,6 +49,24 @@ class CsaqTier(ctypes.Structure):
     ]
 
 
+MAX_RANKS = 8
+IPC_HANDLE_BYTES = 64
+
+
+class CsaqP2PGroup(ctypes.Structure):
+    """Mirror of ``csaq_p2p_group`` (include/csaq_b200.h)."""
+
+    _fields_ = [
+        ("n_ranks", ctypes.c_int32),
+        ("rank", ctypes.c_int32),
+        ("parts", c_vp * MAX_RANKS),
+        ("flags", c_vp * MAX_RANKS),
+        ("seq", c_vp),
+        ("ticket", c_vp),
+        ("err", c_vp),
+    ]
+
+
 # name -> (restype, argtypes)
 _SIGNATURES = {
     "csaq_version": (ctypes.c_char_p, []),
@@ -88,6 +106,14 @@ _SIGNATURES = {
                                              ctypes.c_float, c_vp, c_int, c_vp]),
     "csaq_rank_sum": (c_int, [c_vp, c_int, c_i64, c_i64, c_vp, c_i64, c_i64, c_i64, c_int, c_int, c_vp]),
     "csaq_argmax_parts": (c_int, [c_vp, c_int, c_i64, c_i64, c_i64, c_i64, c_vp, c_int, c_vp]),
+    "csaq_p2p_alloc": (c_int, [c_i64, ctypes.POINTER(c_vp)]),
+    "csaq_p2p_free": (c_int, [c_vp]),
+    "csaq_ipc_handle": (c_int, [c_vp, c_vp]),
+    "csaq_ipc_open": (c_int, [c_vp, ctypes.POINTER(c_vp)]),
+    "csaq_ipc_close": (c_int, [c_vp]),
+    "csaq_tp_exchange_sum": (c_int, [ctypes.POINTER(CsaqP2PGroup), c_i64, c_i64, c_vp, c_i64, c_i64, c_i64, c_int,
+                                     c_vp]),
+    "csaq_p2p_errors": (c_int, [ctypes.POINTER(CsaqP2PGroup), ctypes.POINTER(c_i64)]),
     "csaq_silu_mul": (c_int, [c_vp, c_i64, c_vp, c_i64, c_vp, c_i64, c_i64, c_i64, c_int, c_vp]),
     "csaq_spec_accept": (c_int, [c_vp, c_vp, c_i64, c_i64, c_vp, c_vp, c_vp, c_i64, c_vp, c_vp, c_vp, c_vp, c_vp]),
     "csaq_greedy_commit": (c_int, [c_vp, c_i64, c_vp, c_vp, c_vp, c_i64, c_vp, c_vp, c_vp]),

@@ -28,7 +28,9 @@ rows, in the same launch (see CSAQLinear.gemv_descriptors).
 
 from __future__ import annotations
 
+import ctypes
 import math
+import os
 from dataclasses import dataclass
 from typing import Dict, List, Optional
 
@@ -90,6 +92,91 @@ class _Shape:
     y_part: Optional[torch.Tensor] = None    # TP: this rank's partial o/down output (M, H)
     y_all: Optional[torch.Tensor] = None     # TP: all ranks' partials (W, M, H)
     logits_all: Optional[torch.Tensor] = None  # TP: all ranks' vocabulary slices (W, M, V/W)
+
+
+class _P2PExchange:
+    """Peer-memory buffers for the tensor-parallel combine (csaq_tp_exchange_sum).
+
+    Each rank allocates two partial buffers (rows x H each: parity 0 for the o
+    projection, 1 for down) and a control block (flags, exchange count, CTA
+    ticket, error counter) with csaq_p2p_alloc, sends the IPC handles over the
+    process group, and maps every peer's buffers into its own address space."""
+
+    def __init__(self, group, rank: int, world: int, rows: int, H: int, elem_bytes: int, dev):
+        import torch.distributed as dist
+        if world > _lib.MAX_RANKS:
+            raise ValueError(f"peer-memory combine supports up to {_lib.MAX_RANKS} ranks")
+        L = lib()
+        self.rows, self.H, self.elem = rows, H, elem_bytes
+        self.world, self.rank = world, rank
+        self._own = []
+        self._opened = []
+        parts, ctl = c_void_p_(), c_void_p_()
+        check(L.csaq_p2p_alloc(2 * rows * H * elem_bytes, ctypes.byref(parts)), "p2p_alloc")
+        self._own.append(parts.value)
+        check(L.csaq_p2p_alloc(256, ctypes.byref(ctl)), "p2p_alloc")
+        self._own.append(ctl.value)
+        h0 = (ctypes.c_uint8 * _lib.IPC_HANDLE_BYTES)()
+        h1 = (ctypes.c_uint8 * _lib.IPC_HANDLE_BYTES)()
+        check(L.csaq_ipc_handle(parts.value, h0), "ipc_handle")
+        check(L.csaq_ipc_handle(ctl.value, h1), "ipc_handle")
+        mine = torch.tensor(bytearray(bytes(h0) + bytes(h1)), dtype=torch.uint8, device=dev)
+        allh = torch.empty(world, mine.numel(), dtype=torch.uint8, device=dev)
+        dist.all_gather_into_tensor(allh, mine, group=group)
+        allh = allh.cpu()
+        g = _lib.CsaqP2PGroup()
+        g.n_ranks, g.rank = world, rank
+        for p in range(world):
+            if p == rank:
+                g.parts[p], g.flags[p] = parts.value, ctl.value
+                continue
+            hb = bytes(allh[p].tolist())
+            ptrs = []
+            for k in range(2):
+                buf = (ctypes.c_uint8 * _lib.IPC_HANDLE_BYTES).from_buffer_copy(
+                    hb[k * _lib.IPC_HANDLE_BYTES:(k + 1) * _lib.IPC_HANDLE_BYTES])
+                out = c_void_p_()
+                check(L.csaq_ipc_open(buf, ctypes.byref(out)), "ipc_open")
+                self._opened.append(out.value)
+                ptrs.append(out.value)
+            g.parts[p], g.flags[p] = ptrs[0], ptrs[1]
+        g.seq, g.ticket, g.err = ctl.value + 128, ctl.value + 136, ctl.value + 140
+        self.group = g
+        self.parts_ptr = parts.value
+        dist.barrier(group=group)  # every rank has mapped every peer before any exchange
+
+    def part_ptr(self, parity: int) -> int:
+        return self.parts_ptr + parity * self.rows * self.H * self.elem
+
+    def errors(self) -> int:
+        n = ctypes.c_int64(0)
+        check(lib().csaq_p2p_errors(ctypes.byref(self.group), ctypes.byref(n)), "p2p_errors")
+        return int(n.value)
+
+    def close(self, group=None) -> None:
+        """Unmap the peers' buffers, then (after a barrier over `group`, when
+        given, so that no peer still maps them) free this rank's own."""
+        L = lib()
+        torch.cuda.synchronize()
+        for ptr in self._opened:
+            L.csaq_ipc_close(ptr)
+        self._opened = []
+        if group is not None and self._own:
+            import torch.distributed as dist
+            dist.barrier(group=group)
+        for ptr in self._own:
+            L.csaq_p2p_free(ptr)
+        self._own = []
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+def c_void_p_():
+    return ctypes.c_void_p(0)
 
 
 class DecodeRuntime:
@@ -171,8 +258,21 @@ class DecodeRuntime:
         self.n_out = torch.zeros(B, dtype=i32, device=self.dev)
         self.argmax_buf = torch.zeros(B * (lookahead + 1), dtype=i64, device=self.dev)
         self.shapes: Dict[int, _Shape] = {}
+        # TP combine through peer memory (NVLink), unless CSAQ_TP_EXCHANGE=nccl
+        self.p2p: Optional[_P2PExchange] = None
+        if W > 1 and os.environ.get("CSAQ_TP_EXCHANGE", "p2p") != "nccl":
+            rows = B * max(prefill_chunk, lookahead + 1)
+            self.p2p = _P2PExchange(tp_group, self.tp_rank, W, rows, self.H, self.embed.element_size(), self.dev)
         self.graphs: Dict[str, torch.cuda.CUDAGraph] = {}
         self.launches_per_step: Dict[str, int] = {}
+
+    def release(self) -> None:
+        """Drop the captured graphs and, under TP, the peer-memory buffers
+        (a collective: every rank calls it)."""
+        self.graphs.clear()
+        if self.p2p is not None:
+            self.p2p.close(self.tp_group)
+            self.p2p = None
 
     # ── setup ────────────────────────────────────────────────────────────────
     def _rope_tables(self, inner):
@@ -219,6 +319,10 @@ class DecodeRuntime:
                 gu = (mods["gate"].gemv_descriptors(sh.gu[:, :I], verify)
                       + mods["up"].gemv_descriptors(sh.gu[:, I:], verify))
                 dn = mods["down"].gemv_descriptors(res_out, verify, residual=res)
+                if self._p2p_for(M):  # partials straight into the peer-visible buffers
+                    for parity, ds in ((0, o), (1, dn)):
+                        for d in ds:
+                            d.y, d.ldy = self.p2p.part_ptr(parity), H
                 for name, d in (("qkv", qkv), ("o", o), ("gu", gu), ("down", dn)):
                     sh.descs[(li, name, verify)] = (_lib.tier_array(d), len(d))
         d = self.lm_head.gemv_descriptors(sh.logits)
@@ -238,8 +342,17 @@ class DecodeRuntime:
         else:
             check(lib().csaq_qgemv(arr, n, K, x.data_ptr(), self.dt, M, x.stride(0), st), "qgemv")
 
-    def _combine(self, sh: _Shape, M: int, st: int) -> None:
-        """TP: gather every rank's partial o/down output and add them to x in rank order."""
+    def _p2p_for(self, M: int) -> bool:
+        return self.p2p is not None and M <= self.p2p.rows
+
+    def _combine(self, sh: _Shape, M: int, st: int, parity: int) -> None:
+        """TP: add every rank's partial o (parity 0) or down (parity 1) output
+        to x in rank order: through peer memory when the step fits the
+        exchange buffers, else an NCCL all-gather and csaq_rank_sum."""
+        if self._p2p_for(M):
+            check(lib().csaq_tp_exchange_sum(ctypes.byref(self.p2p.group), parity * self.p2p.rows * self.H, self.H,
+                                             sh.x.data_ptr(), self.H, M, self.H, self.dt, st), "tp_exchange")
+            return
         import torch.distributed as dist
         dist.all_gather_into_tensor(sh.y_all[:, :M], sh.y_part[:M], group=self.tp_group)
         H = self.H
@@ -301,7 +414,7 @@ class DecodeRuntime:
             self._attention(li, sh, S, pos, pos_host, scale, st)
             self._gemv(sh.descs[(li, "o", verify)], nq, sh.attn, M, st)
             if self.tp > 1:
-                self._combine(sh, M, st)
+                self._combine(sh, M, st, 0)
             check(L.csaq_rmsnorm(sh.x.data_ptr(), H, layer.post_attention_layernorm.weight.data_ptr(),
                                  sh.xn.data_ptr(), H, M, H, self.eps, self.dt, st), "rmsnorm")
             self._gemv(sh.descs[(li, "gu", verify)], H, sh.xn, M, st)
@@ -309,7 +422,7 @@ class DecodeRuntime:
                                   sh.gu.stride(0), sh.h.data_ptr(), I, M, I, self.dt, st), "silu_mul")
             self._gemv(sh.descs[(li, "down", verify)], I, sh.h, M, st)
             if self.tp > 1:
-                self._combine(sh, M, st)
+                self._combine(sh, M, st, 1)
         check(L.csaq_rmsnorm(sh.x.data_ptr(), H, self.final_norm.data_ptr(), sh.xn.data_ptr(), H, M, H,
                              self.eps, self.dt, st), "rmsnorm")
         if last_only and S > 1:
@@ -355,6 +468,29 @@ class DecodeRuntime:
         2 rank-order combines under TP); plus the final RMSNorm, the lm_head
         GEMV and the argmax."""
         return self.n_layers * (9 + (2 if self.tp > 1 else 0)) + 3
+
+    def prefill_kernels(self, P: int, verify: bool = True) -> int:
+        """Own kernel launches of reset() for a P-token prompt: per chunk and
+        layer 2 RMSNorm, RoPE, SiLU, the decode attention kernel for chunks
+        below PREFILL_SDPA_TOKENS (torch's fused attention above), the
+        combines under TP, and the linears (one tcgen05 GEMM launch per tier
+        from RUNTIME_GEMM_MIN_TOKENS tokens, else one GEMV launch per 16 tokens
+        or fewer); then the final RMSNorm, the lm_head GEMV and the argmax."""
+        n, C = 0, self.prefill_chunk
+        for s0 in range(0, P, C):
+            S = min(C, P - s0)
+            M = self.B * S
+            sh = self._shape(S)
+            for li in range(self.n_layers):
+                for name in ("qkv", "o", "gu", "down"):
+                    arr, nd = sh.descs[(li, name, verify)]
+                    if M >= RUNTIME_GEMM_MIN_TOKENS:
+                        n += sum(1 for i in range(nd) if arr[i].n_rows > 0)
+                    else:
+                        n += -(-M // 16)
+                n += 4 + (0 if S >= PREFILL_SDPA_TOKENS else 1) + (2 if self.tp > 1 else 0)
+            n += 2
+        return n + 1
 
     # ── generation ──────────────────────────────────────────────────────────
     @torch.no_grad()

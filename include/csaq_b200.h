@@ -246,6 +246,41 @@ int csaq_decode_attention(const void* q, const void* k_cache, const void* v_cach
 int csaq_rank_sum(const void* parts, int n_parts, int64_t part_stride, int64_t ld_parts, void* out,
                   int64_t ldo, int64_t M, int64_t N, int add_out, int dtype, void* stream);
 
+/* ── Tensor-parallel combine over NVLink peer memory ─────────────────────
+ * No counterpart in the reference (it has no multi-GPU path); these replace
+ * the NCCL all-gather + csaq_rank_sum pair after the row-split o/down
+ * projections with one kernel per rank that reads the peers' partials over
+ * NVLink. Buffers come from csaq_p2p_alloc (cudaMalloc, zeroed) and are
+ * mapped into the other ranks' processes with csaq_ipc_handle/csaq_ipc_open
+ * (the handles travel over the caller's process group). */
+#define CSAQ_MAX_RANKS 8
+#define CSAQ_IPC_HANDLE_BYTES 64
+
+typedef struct csaq_p2p_group {
+  int32_t n_ranks, rank;
+  const void* parts[CSAQ_MAX_RANKS]; /* rank r's partial buffer, as mapped in this process */
+  uint64_t* flags[CSAQ_MAX_RANKS];   /* rank r's flag array (n_ranks u64), as mapped here  */
+  uint64_t* seq;                     /* this rank's exchange count (device, starts at 0)   */
+  uint32_t* ticket;                  /* this rank's CTA ticket (device, starts at 0)       */
+  uint32_t* err;                     /* this rank's abandoned-wait counter (device)        */
+} csaq_p2p_group;
+
+int csaq_p2p_alloc(int64_t bytes, void** ptr);
+int csaq_p2p_free(void* ptr);
+int csaq_ipc_handle(const void* ptr, uint8_t* handle);
+int csaq_ipc_open(const uint8_t* handle, void** ptr);
+int csaq_ipc_close(void* ptr);
+
+/* out[m, n] = T(out[m, n] + sum over r of parts[r][part_offset + m*ld_parts + n])
+ * in fp32, in rank order: csaq_rank_sum over the ranks' own buffers. Every
+ * rank launches it for the same exchange in the same order; it signals the
+ * peers that this rank's partial is complete and waits (bounded; an
+ * abandoned wait counts in *err, read with csaq_p2p_errors) for theirs. A
+ * rank may rewrite a partial buffer only after the next exchange. */
+int csaq_tp_exchange_sum(const csaq_p2p_group* group, int64_t part_offset, int64_t ld_parts, void* out,
+                         int64_t ldo, int64_t M, int64_t N, int dtype, void* stream);
+int csaq_p2p_errors(const csaq_p2p_group* group, int64_t* count);
+
 /* Greedy token of each row: the global index of the largest logit over
  * n_parts vocabulary slices of part_len values (slice r at r*part_stride,
  * rows ld apart), the smallest index on ties; torch.argmax of the sampler

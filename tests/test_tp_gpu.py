@@ -3,7 +3,9 @@
 Two NCCL ranks run a quantised tiny Llama through DecodeRuntime with a TP
 group: the prefill logits match the single-GPU runtime's within 3e-2 (the
 partial sums are added in a different order), and greedy self-speculative
-output equals greedy decoding with the verify weights under TP.
+output equals greedy decoding with the verify weights under TP. The combine
+after the row-split projections goes through peer memory (csaq_tp_exchange_sum,
+no abandoned waits) and gives bitwise the results of the NCCL all-gather path.
 """
 
 import os
@@ -48,6 +50,7 @@ def _worker(rank, world, port, q):
         model, _ = _build(dev)
         prompt = torch.randint(0, 2048, (1, 40), generator=torch.Generator().manual_seed(6)).to(dev)
         rt = DecodeRuntime(model, 1, 256, 4, tp_group=dist.group.WORLD)
+        out["peer_memory"] = rt.p2p is not None
         rt.reset(prompt, 24, verify=True)
         out["tp_logits"] = rt.prefill_logits.float().cpu()
         rt.generate_greedy(24, verify=True)
@@ -55,8 +58,19 @@ def _worker(rank, world, port, q):
         rt.reset(prompt, 24, verify=True)
         rt.generate_speculative(24)
         out["spec_equals_greedy"] = torch.equal(rt.outputs().cpu()[:, :24], greedy[:, :24])
-        rt.graphs.clear()
+        out["p2p_errors"] = rt.p2p.errors() if rt.p2p is not None else -1
+        rt.release()
         del rt
+        # the NCCL all-gather combine adds the same partials in the same order
+        os.environ["CSAQ_TP_EXCHANGE"] = "nccl"
+        rt2 = DecodeRuntime(model, 1, 256, 4, tp_group=dist.group.WORLD)
+        rt2.reset(prompt, 24, verify=True)
+        out["nccl_logits_equal"] = torch.equal(rt2.prefill_logits.float().cpu(), out["tp_logits"])
+        rt2.generate_greedy(24, verify=True)
+        out["nccl_greedy_equal"] = torch.equal(rt2.outputs().cpu()[:, :24], greedy[:, :24])
+        rt2.release()
+        del rt2
+        os.environ.pop("CSAQ_TP_EXCHANGE")
         torch.cuda.synchronize()
         if rank == 0:
             one = DecodeRuntime(model, 1, 256, 4)
@@ -84,6 +98,9 @@ def test_tensor_parallel_runtime_two_gpus():
         assert p.exitcode == 0
     for r in (0, 1):
         assert res[r]["spec_equals_greedy"], r
+        assert res[r]["peer_memory"], r
+        assert res[r]["p2p_errors"] == 0, r
+        assert res[r]["nccl_logits_equal"] and res[r]["nccl_greedy_equal"], r
     a, b = res[0]["tp_logits"], res[0]["tp1_logits"]
     assert torch.equal(res[0]["tp_logits"], res[1]["tp_logits"])
     err = float((a - b).norm() / b.norm())
