@@ -106,6 +106,10 @@ _SIGNATURES = {
                                              ctypes.c_float, c_vp, c_int, c_vp]),
     "csaq_rank_sum": (c_int, [c_vp, c_int, c_i64, c_i64, c_vp, c_i64, c_i64, c_i64, c_int, c_int, c_vp]),
     "csaq_argmax_parts": (c_int, [c_vp, c_int, c_i64, c_i64, c_i64, c_i64, c_vp, c_int, c_vp]),
+    "csaq_sample_rows": (c_int, [c_vp, c_int, c_i64, c_i64, c_i64, c_i64, ctypes.c_float, ctypes.c_float,
+                                 ctypes.c_uint64, c_vp, c_vp, c_int, c_vp]),
+    "csaq_spec_sample_verify": (c_int, [c_vp, c_vp, c_vp, c_int, c_i64, c_i64, c_i64, c_i64, c_i64,
+                                        ctypes.c_float, ctypes.c_float, ctypes.c_uint64, c_vp, c_vp, c_int, c_vp]),
     "csaq_p2p_alloc": (c_int, [c_i64, ctypes.POINTER(c_vp)]),
     "csaq_p2p_free": (c_int, [c_vp]),
     "csaq_ipc_handle": (c_int, [c_vp, c_vp]),

@@ -230,10 +230,12 @@ class CSAQInferenceEngine:
             print("[CSAQ] Inference engine warmup complete.")
 
     # ── fast path ───────────────────────────────────────────────────────────
-    def _fast_ok(self, input_ids: torch.Tensor, temperature: float) -> bool:
+    def _fast_ok(self, input_ids: torch.Tensor, temperature: float, speculative: bool = False) -> bool:
+        """The static runtime serves greedy decoding and, at temperature > 0,
+        self-speculative sampling (on-device rejection sampling)."""
         from . import runtime
-        return (temperature == 0.0 and torch.cuda.is_available() and input_ids is not None
-                and input_ids.dim() == 2 and runtime.supports(self.model))
+        return ((temperature == 0.0 or (speculative and bool(self._hooks))) and torch.cuda.is_available()
+                and input_ids is not None and input_ids.dim() == 2 and runtime.supports(self.model))
 
     def runtime(self, batch: int, max_len: int, lookahead: int):
         """The (cached) static decode runtime for this batch / length / lookahead."""
@@ -251,17 +253,20 @@ class CSAQInferenceEngine:
         return rt
 
     def _generate_fast(self, input_ids: torch.Tensor, speculative: bool, lookahead: int,
-                       max_new_tokens: int) -> Tuple[torch.Tensor, SpeculativeReport]:
+                       max_new_tokens: int, temperature: float = 0.0, top_p: float = 1.0,
+                       seed: Optional[int] = None) -> Tuple[torch.Tensor, SpeculativeReport]:
         B, P = input_ids.shape
         K = max(1, lookahead)
         rt = self.runtime(B, P + max_new_tokens + 2 * K + 2, K)
         ids_dev = input_ids.to(self.device, non_blocking=True)
         t0 = time.time()
-        rt.reset(ids_dev, max_new_tokens, verify=speculative)
+        if seed is None:
+            seed = int(torch.randint(0, 2 ** 62, (1,)).item()) if temperature > 0.0 else 0
+        rt.reset(ids_dev, max_new_tokens, verify=speculative, temperature=temperature, top_p=top_p, seed=seed)
         report = SpeculativeReport(mode="speculative" if speculative else "standard")
         if max_new_tokens > 1:
             if speculative:
-                iters = rt.generate_speculative(max_new_tokens)
+                iters = rt.generate_speculative(max_new_tokens, temperature=temperature, top_p=top_p, seed=seed)
                 st = rt.spec_stats()
                 report.draft_calls = iters * K
                 report.verify_calls = iters
@@ -285,10 +290,11 @@ class CSAQInferenceEngine:
     def generate(self, input_ids: Optional[torch.Tensor] = None, *, speculative: bool = False,
                  lookahead: int = 4, temperature: float = 1.0, top_p: float = 1.0,
                  max_new_tokens: int = 128, **kwargs: Any) -> Tuple[torch.Tensor, SpeculativeReport]:
-        if input_ids is not None and self._fast_ok(input_ids, temperature):
+        if input_ids is not None and self._fast_ok(input_ids, temperature, speculative):
             with torch.no_grad():
                 return self._generate_fast(input_ids, speculative and bool(self._hooks), lookahead,
-                                           max_new_tokens)
+                                           max_new_tokens, temperature=temperature, top_p=top_p,
+                                           seed=kwargs.get("seed"))
         if speculative and self._hooks:
             return self._generate_speculative(input_ids, max_new_tokens, lookahead, temperature, top_p)
         self._ensure_draft_state()

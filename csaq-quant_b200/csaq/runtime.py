@@ -257,6 +257,10 @@ class DecodeRuntime:
         self.out_tokens = torch.zeros(B, self.cap, dtype=i64, device=self.dev)
         self.n_out = torch.zeros(B, dtype=i32, device=self.dev)
         self.argmax_buf = torch.zeros(B * (lookahead + 1), dtype=i64, device=self.dev)
+        # sampling at temperature > 0: Philox call counter (+ CTA ticket), the
+        # draft steps' full-vocabulary logits (allocated on first use)
+        self.rng = torch.zeros(2, dtype=i64, device=self.dev)
+        self.dlog: Optional[torch.Tensor] = None
         self.shapes: Dict[int, _Shape] = {}
         # TP combine through peer memory (NVLink), unless CSAQ_TP_EXCHANGE=nccl
         self.p2p: Optional[_P2PExchange] = None
@@ -494,9 +498,11 @@ class DecodeRuntime:
 
     # ── generation ──────────────────────────────────────────────────────────
     @torch.no_grad()
-    def reset(self, prompts: torch.Tensor, max_new: int, verify: bool = True) -> None:
+    def reset(self, prompts: torch.Tensor, max_new: int, verify: bool = True, temperature: float = 0.0,
+              top_p: float = 1.0, seed: int = 0) -> None:
         """Prefill `prompts` (B, P) (verify or draft weights) and set the state
-        for generating `max_new` tokens (the first comes from the prefill)."""
+        for generating `max_new` tokens (the first comes from the prefill:
+        greedy at temperature 0, else sampled)."""
         B, P = prompts.shape
         if B != self.B:
             raise ValueError(f"runtime built for batch {self.B}, got {B}")
@@ -514,7 +520,11 @@ class DecodeRuntime:
             self.pos0.fill_(s0)
             self.step(S, chunk.contiguous().view(-1), self.pos0, verify=verify, last_only=True, pos_host=s0)
         self.prefill_logits = self.logits_full(S, self.B)
-        self.argmax(S, self.B, self.next_tok)
+        self.rng.zero_()
+        if temperature > 0.0:
+            self.sample(S, self.B, self.next_tok, temperature, top_p, seed)
+        else:
+            self.argmax(S, self.B, self.next_tok)
         self.out_tokens[:, 0] = self.next_tok
         self.n_out.fill_(1)
         self.pos0.fill_(P)
@@ -540,6 +550,60 @@ class DecodeRuntime:
                                  self.out_tokens.data_ptr(), self.n_out.data_ptr(), self.cap,
                                  self.next_tok.data_ptr(), self.n_new.data_ptr(), self.stats.data_ptr(),
                                  self.remaining.data_ptr(), st), "spec_accept")
+
+    def _logit_parts(self, S: int, rows: int):
+        """(pointer, n_parts, part_stride, ld, part_len) of the first `rows`
+        full-vocabulary logit rows of the last step (gathered under TP)."""
+        sh = self.shapes[S]
+        if self.tp > 1:
+            src = self._gather_logits(sh, rows)
+            return src.data_ptr(), self.tp, rows * self.Vl, self.Vl, self.Vl
+        return sh.logits.data_ptr(), 1, 0, self.Vl, self.Vl
+
+    def sample(self, S: int, rows: int, out: torch.Tensor, temperature: float, top_p: float, seed: int) -> None:
+        """Draw one token per logit row of the last step (csaq_sample_rows)."""
+        st = torch.cuda.current_stream(self.dev).cuda_stream
+        ptr, n_parts, pstride, ld, plen = self._logit_parts(S, rows)
+        check(lib().csaq_sample_rows(ptr, n_parts, pstride, ld, plen, rows, float(temperature), float(top_p),
+                                     int(seed) & 0xFFFFFFFFFFFFFFFF, self.rng.data_ptr(), out.data_ptr(), self.dt,
+                                     st), "sample")
+
+    def _spec_iteration_sample(self, temperature: float, top_p: float, seed: int) -> None:
+        """One self-speculative iteration with sampled drafts and on-device
+        rejection sampling (no host synchronisation)."""
+        K, B, V = self.K, self.B, self.V
+        L = lib()
+        st = torch.cuda.current_stream(self.dev).cuda_stream
+        if self.dlog is None or self.dlog.shape != (K, B, V):
+            self.dlog = torch.zeros(K, B, V, dtype=self.dtype, device=self.dev)
+        self.vin[:, 0].copy_(self.next_tok)
+        self.cur_pos.copy_(self.pos0)
+        for k in range(K):
+            self.step(1, self.next_tok, self.cur_pos, verify=False)
+            self.dlog[k].copy_(self.logits_view(1, B))
+            check(L.csaq_sample_rows(self.dlog[k].data_ptr(), 1, 0, V, V, B, float(temperature), float(top_p),
+                                     int(seed) & 0xFFFFFFFFFFFFFFFF, self.rng.data_ptr(), self.next_tok.data_ptr(),
+                                     self.dt, st), "sample")
+            self.draft[:, k].copy_(self.next_tok)
+            self.vin[:, k + 1].copy_(self.next_tok)
+            self.cur_pos.add_(1)
+        self.step(K + 1, self.vin, self.pos0, verify=True)
+        ptr, n_parts, pstride, ld, plen = self._logit_parts(K + 1, B * (K + 1))
+        check(L.csaq_spec_sample_verify(self.draft.data_ptr(), self.dlog.data_ptr(), ptr, n_parts, pstride, ld, plen,
+                                        B, K, float(temperature), float(top_p), int(seed) & 0xFFFFFFFFFFFFFFFF,
+                                        self.rng.data_ptr(), self.vt.data_ptr(), self.dt, st), "spec_sample")
+        check(L.csaq_spec_accept(self.draft.data_ptr(), self.vt.data_ptr(), B, K, self.pos0.data_ptr(),
+                                 self.out_tokens.data_ptr(), self.n_out.data_ptr(), self.cap,
+                                 self.next_tok.data_ptr(), self.n_new.data_ptr(), self.stats.data_ptr(),
+                                 self.remaining.data_ptr(), st), "spec_accept")
+
+    def logits_view(self, S: int, rows: int) -> torch.Tensor:
+        """The first `rows` full-vocabulary logit rows of the last step as a
+        (rows, V) tensor (a view at TP 1; gathered and rearranged under TP)."""
+        sh = self.shapes[S]
+        if self.tp == 1:
+            return sh.logits[:rows]
+        return self._gather_logits(sh, rows).permute(1, 0, 2).reshape(rows, self.V)
 
     @torch.no_grad()
     def _greedy_step(self, verify: bool) -> None:
@@ -573,11 +637,17 @@ class DecodeRuntime:
 
     def _state(self) -> List[torch.Tensor]:
         return [self.pos0, self.cur_pos, self.next_tok, self.draft, self.vin, self.vt, self.n_new,
-                self.stats, self.remaining, self.out_tokens, self.n_out, self.k_cache, self.v_cache]
+                self.stats, self.remaining, self.out_tokens, self.n_out, self.k_cache, self.v_cache, self.rng]
 
-    def generate_speculative(self, max_new: int) -> int:
-        """Self-speculative greedy decode after reset(); returns iterations."""
-        g = self._graph("spec", self._spec_iteration)
+    def generate_speculative(self, max_new: int, temperature: float = 0.0, top_p: float = 1.0,
+                             seed: int = 0) -> int:
+        """Self-speculative decode after reset(); greedy at temperature 0, else
+        sampled drafts with on-device rejection sampling; returns iterations."""
+        if temperature > 0.0:
+            key = f"spec_sample_{temperature!r}_{top_p!r}_{seed}"
+            g = self._graph(key, lambda: self._spec_iteration_sample(temperature, top_p, seed))
+        else:
+            g = self._graph("spec", self._spec_iteration)
         iters = 0
         rem_host = torch.empty(1, dtype=torch.int32, pin_memory=True)
         while True:

@@ -322,6 +322,23 @@ int csaq_spec_accept(const int64_t* draft, const int64_t* verify_argmax, int64_t
                      int64_t* next_tok, int32_t* n_new, int64_t* stats, int32_t* remaining,
                      void* stream);
 
+/* ── Sampling at temperature > 0 (csaq/inference.py:269-304, :482-518) ────
+ * Logit rows are given as n_parts vocabulary slices of part_len values
+ * (slice r at r*part_stride, rows ld apart; one part for a single GPU).
+ * counter: two u64 in device memory, zero before the first call; each call
+ * advances counter[0] so that graph replays draw new numbers (Philox, seed). */
+int csaq_sample_rows(const void* logits, int n_parts, int64_t part_stride, int64_t ld, int64_t part_len,
+                     int64_t rows, float temperature, float top_p, uint64_t seed, uint64_t* counter, int64_t* out,
+                     int dtype, void* stream);
+/* vt (B x (K+1)) for csaq_spec_accept from the draft tokens (B x K), the
+ * draft steps' full-vocabulary logits (K x B x V, contiguous) and the verify
+ * logits (rows b*(K+1)+k): rejection sampling of each draft token, a residual
+ * draw at the first rejection, a bonus draw when all are accepted. */
+int csaq_spec_sample_verify(const int64_t* draft, const void* draft_logits, const void* verify_logits, int n_parts,
+                            int64_t part_stride, int64_t ld, int64_t part_len, int64_t B, int64_t K,
+                            float temperature, float top_p, uint64_t seed, uint64_t* counter, int64_t* vt,
+                            int dtype, void* stream);
+
 /* Bookkeeping of one plain greedy decode step. */
 int csaq_greedy_commit(const int64_t* tok, int64_t B, int32_t* pos0, int64_t* out_tokens,
                        int32_t* n_out, int64_t cap, int64_t* next_tok, int32_t* remaining,
