@@ -26,7 +26,8 @@
 //     so a token's result is bitwise independent of how many tokens share the
 //     launch.
 //   * Activations are staged once per CTA as fp16 MMA B-fragments ("records"),
-//     scaled per token by a power of two (exact for bf16 / fp16 inputs).
+//     scaled per (128-column chunk, token) by a power of two (exact for bf16 /
+//     fp16 inputs; the factor is applied to the chunk's partial sum).
 //   * Codes become fp16 MMA operands with one LOP3 per register: a nibble
 //     OR-ed into the mantissa of 1024.0 gives 1024 + f*q (f = 1 or 16 by the
 //     nibble's position; 2-bit codes: 1, 4, 16, 64); the matching record entry
@@ -181,18 +182,11 @@ __global__ void repack_meta_kernel(const csaq_tier T, int64_t n_chunks, int64_t 
 // R2 (2-bit tiers), word m = cols 16m..16m+15, t = 0..3:
 //   [4m+t] = ((x_{2t}/f,x_{2t+8}/f),(x_{2t+1}/f',x_{2t+9}/f')), (f,f') = (1,4),(16,64),(1,4),(16,64)
 //   C2 = sum (1024 / f) x
-template <typename ACT>
-__device__ __forceinline__ void build_records(const ACT* __restrict__ xrow, float inv, bool want2,
-                                              uint2 (&r4)[8], uint2 (&r2)[8], float& C4, float& C2,
-                                              float& S) {
+__device__ __forceinline__ void build_records(const float (&xv)[32], float inv, bool want2, uint2 (&r4)[8],
+                                              uint2 (&r2)[8], float& C4, float& C2, float& S) {
   float v[32];
 #pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const uint4 q = ld_cached_v4(xrow + 8 * i);
-    const ACT* e = reinterpret_cast<const ACT*>(&q);
-#pragma unroll
-    for (int j = 0; j < 8; ++j) v[8 * i + j] = to_f32<ACT>(e[j]) * inv;  // exact power-of-two scaling
-  }
+  for (int i = 0; i < 32; ++i) v[i] = xv[i] * inv;  // exact power-of-two scaling
   float c4 = 0.0f, s = 0.0f;
 #pragma unroll
   for (int m = 0; m < 4; ++m) {
@@ -467,10 +461,10 @@ __device__ __forceinline__ void chunk_math(const uint8_t* slot, const uint8_t* r
           const float z0 = (float)meta[64 + g], z1 = (float)meta[64 + g + 8];
           const float d0 = gg[mt][0][0] + gg[mt][1][0], d1 = gg[mt][0][1] + gg[mt][1][1];
           const float d2 = gg[mt][0][2] + gg[mt][1][2], d3 = gg[mt][0][3] + gg[mt][1][3];
-          acc[mt][nt][0] = fmaf(s0, fmaf(-z0, cs0.y, d0 - cs0.x), acc[mt][nt][0]);
-          acc[mt][nt][1] = fmaf(s0, fmaf(-z0, cs1.y, d1 - cs1.x), acc[mt][nt][1]);
-          acc[mt][nt][2] = fmaf(s1, fmaf(-z1, cs0.y, d2 - cs0.x), acc[mt][nt][2]);
-          acc[mt][nt][3] = fmaf(s1, fmaf(-z1, cs1.y, d3 - cs1.x), acc[mt][nt][3]);
+          acc[mt][nt][0] = fmaf(s0 * cs0.w, fmaf(-z0, cs0.y, d0 - cs0.x), acc[mt][nt][0]);
+          acc[mt][nt][1] = fmaf(s0 * cs1.w, fmaf(-z0, cs1.y, d1 - cs1.x), acc[mt][nt][1]);
+          acc[mt][nt][2] = fmaf(s1 * cs0.w, fmaf(-z1, cs0.y, d2 - cs0.x), acc[mt][nt][2]);
+          acc[mt][nt][3] = fmaf(s1 * cs1.w, fmaf(-z1, cs1.y, d3 - cs1.x), acc[mt][nt][3]);
         }
       } else {
         const uint8_t* meta = slot + code_bytes(8);
@@ -483,10 +477,10 @@ __device__ __forceinline__ void chunk_math(const uint8_t* slot, const uint8_t* r
           const float C = (e & 1) ? cs1.x : cs0.x;
           d[e] = fmaf(16.0f, hi - C, lo - C);
         }
-        acc[0][nt][0] = fmaf(s0, fmaf(-z0, cs0.y, d[0]), acc[0][nt][0]);
-        acc[0][nt][1] = fmaf(s0, fmaf(-z0, cs1.y, d[1]), acc[0][nt][1]);
-        acc[0][nt][2] = fmaf(s1, fmaf(-z1, cs0.y, d[2]), acc[0][nt][2]);
-        acc[0][nt][3] = fmaf(s1, fmaf(-z1, cs1.y, d[3]), acc[0][nt][3]);
+        acc[0][nt][0] = fmaf(s0 * cs0.w, fmaf(-z0, cs0.y, d[0]), acc[0][nt][0]);
+        acc[0][nt][1] = fmaf(s0 * cs1.w, fmaf(-z0, cs1.y, d[1]), acc[0][nt][1]);
+        acc[0][nt][2] = fmaf(s1 * cs0.w, fmaf(-z1, cs0.y, d[2]), acc[0][nt][2]);
+        acc[0][nt][3] = fmaf(s1 * cs1.w, fmaf(-z1, cs1.y, d[3]), acc[0][nt][3]);
       }
     } else if constexpr (bits == 16) {
       uint32_t cw[2][16];
@@ -501,7 +495,7 @@ __device__ __forceinline__ void chunk_math(const uint8_t* slot, const uint8_t* r
         }
       mma16(cw, rec, gg);
 #pragma unroll
-      for (int e = 0; e < 4; ++e) acc[0][nt][e] += gg[0][e] + gg[1][e];
+      for (int e = 0; e < 4; ++e) acc[0][nt][e] = fmaf(gg[0][e] + gg[1][e], (e & 1) ? cs1.w : cs0.w, acc[0][nt][e]);
     } else {  // 2-bit
       uint32_t cw[2][2][2];
       float gg[2][2][4];
@@ -524,10 +518,10 @@ __device__ __forceinline__ void chunk_math(const uint8_t* slot, const uint8_t* r
         const float z0 = (float)meta[64 + g], z1 = (float)meta[64 + g + 8];
         const float d0 = gg[mt][0][0] + gg[mt][1][0], d1 = gg[mt][0][1] + gg[mt][1][1];
         const float d2 = gg[mt][0][2] + gg[mt][1][2], d3 = gg[mt][0][3] + gg[mt][1][3];
-        acc[mt][nt][0] = fmaf(s0, fmaf(-z0, cs0.y, d0 - cs0.z), acc[mt][nt][0]);
-        acc[mt][nt][1] = fmaf(s0, fmaf(-z0, cs1.y, d1 - cs1.z), acc[mt][nt][1]);
-        acc[mt][nt][2] = fmaf(s1, fmaf(-z1, cs0.y, d2 - cs0.z), acc[mt][nt][2]);
-        acc[mt][nt][3] = fmaf(s1, fmaf(-z1, cs1.y, d3 - cs1.z), acc[mt][nt][3]);
+        acc[mt][nt][0] = fmaf(s0 * cs0.w, fmaf(-z0, cs0.y, d0 - cs0.z), acc[mt][nt][0]);
+        acc[mt][nt][1] = fmaf(s0 * cs1.w, fmaf(-z0, cs1.y, d1 - cs1.z), acc[mt][nt][1]);
+        acc[mt][nt][2] = fmaf(s1 * cs0.w, fmaf(-z1, cs0.y, d2 - cs0.z), acc[mt][nt][2]);
+        acc[mt][nt][3] = fmaf(s1 * cs1.w, fmaf(-z1, cs1.y, d3 - cs1.z), acc[mt][nt][3]);
       }
     }
   }
@@ -597,33 +591,9 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kThreads, 1)
   for (int d = 0; d < P.depth; ++d) issue();  // weights first: no kernel writes them
   pdl_wait();  // x (and y, bias, residual) may come from the previous kernel of the stream
 
-  // token scales: e_t with max|x_t| * 2^-e_t in [2^14, 2^15)
-  uint32_t* smax = reinterpret_cast<uint32_t*>(xexp);
-  if (threadIdx.x < 16) smax[threadIdx.x] = 0u;
-  __syncthreads();
-  const int k8 = (int)(K / 8);
-  {  // the tokens side by side: warp w scans part w / M of token w % M (M <= kWarps)
-    const int wpt = kWarps / M, tok = warp % M, part = warp / M;
-    if (part < wpt) {
-      float mx = 0.0f;
-      for (int kk = part * 32 + lane; kk < k8; kk += wpt * 32) {
-        const uint4 q = ld_cached_v4(x + (int64_t)tok * ldx + 8 * kk);
-        const ACT* e = reinterpret_cast<const ACT*>(&q);
-#pragma unroll
-        for (int j = 0; j < 8; ++j) mx = fmaxf(mx, fabsf(to_f32<ACT>(e[j])));
-      }
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-      if (lane == 0 && mx > 0.0f) atomicMax(&smax[tok], __float_as_uint(mx));
-    }
-  }
-  __syncthreads();
-  if (threadIdx.x < 16) {
-    const uint32_t b = smax[threadIdx.x];
-    const int E = (int)((b >> 23) & 0xFF) - 127;
-    xexp[threadIdx.x] = ldexpf(1.0f, b == 0u ? 0 : E - 14);  // 2^e: the output factor
-  }
-  __syncthreads();
+  // the power-of-two scales are per (chunk, token): no pass over x before
+  // the records; the output factor is applied per chunk in the main loop
+  if (threadIdx.x < 16) xexp[threadIdx.x] = 1.0f;
 
   // activation records (whole warps iterate: 4-lane shuffles); split: this
   // CTA builds and holds the records of its own chunk half only
@@ -638,8 +608,27 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kThreads, 1)
     const int tok = live ? rest % M : 0, li = live ? rest / M : 0, ch = c_lo + li;
     uint2 r4[8], r2[8];
     float C4 = 0.0f, C2 = 0.0f, S = 0.0f;
-    if (live) build_records<ACT>(x + (int64_t)tok * ldx + ch * 128 + cc * 32, 1.0f / xexp[tok],
-                                 P.want2 != 0, r4, r2, C4, C2, S);
+    // this lane's 32 columns, then the chunk's scale 2^e (max|x| * 2^-e in
+    // [2^14, 2^15), exact for bf16/fp16) from the 4 lanes of the (chunk, token)
+    float xv[32];
+    float mx = 0.0f;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const uint4 q = live ? ld_cached_v4(x + (int64_t)tok * ldx + ch * 128 + cc * 32 + 8 * i)
+                           : make_uint4(0u, 0u, 0u, 0u);
+      const ACT* e = reinterpret_cast<const ACT*>(&q);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        xv[8 * i + j] = to_f32<ACT>(e[j]);
+        mx = fmaxf(mx, fabsf(xv[8 * i + j]));
+      }
+    }
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+    const uint32_t mb = __float_as_uint(mx);
+    const int E = mb == 0u ? 14 : (int)((mb >> 23) & 0xFF) - 127;
+    const float fac = ldexpf(1.0f, E - 14);
+    if (live) build_records(xv, 1.0f / fac, P.want2 != 0, r4, r2, C4, C2, S);
 #pragma unroll
     for (int o = 1; o < 4; o <<= 1) {
       C4 += __shfl_xor_sync(0xffffffffu, C4, o);
@@ -655,7 +644,7 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kThreads, 1)
 #pragma unroll
         for (int j = 0; j < 8; ++j) d2[4 * j] = r2[j];
       }
-      if (cc == 0) xcs[li * M + tok] = make_float4(C4, S, C2, 0.0f);
+      if (cc == 0) xcs[li * M + tok] = make_float4(C4, S, C2, fac);
     }
   }
   if constexpr (SPLIT)
