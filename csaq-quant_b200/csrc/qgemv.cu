@@ -374,6 +374,14 @@ constexpr int kCluster = 2;  // CTAs per cluster: a unit's partial sums never le
 __device__ __forceinline__ void cluster_sync() {
   asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
+// the two halves of cluster_sync; `dep` is an unused operand that orders the
+// arrive after the computation of its value
+__device__ __forceinline__ void cluster_arrive_after(float dep) {
+  asm volatile("barrier.cluster.arrive.release.aligned;" ::"f"(dep) : "memory");
+}
+__device__ __forceinline__ void cluster_wait() {
+  asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
 // the shared::cluster address of `saddr` (a local shared address) in CTA `rank` of the cluster
 __device__ __forceinline__ uint32_t dsmem_addr(uint32_t saddr, int rank) {
   uint32_t r;
@@ -774,26 +782,23 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kThreads, 1)
     const int v = __shfl_sync(0xffffffffu, b_lane, (w - cl_base) & 31);
     return w - cl_base == 32 ? b_end : v;
   };
-#pragma unroll 1
-  for (int s = 0; s < 2; ++s) {
-    const int ut = s == 0 ? cut_t0 : cut_t1;
-    if (ut < 0) continue;
-    const int unit = s == 0 ? cut_u0 : cut_u1;
-    const int u_start = s == 0 ? cut_s0 : cut_s1, u_end = u_start + n_chunks;
-    // units never cross a cluster boundary; the highest warp holding part of
-    // the unit adds the partials in warp order and writes y
-    if (begin_of(wg + 1) < u_end) continue;
-    const TierWork& tw = P.w[ut];
-    const csaq_tier& T = P.tp.t[ut];
-    const int rows = tw.mt * kTileRows;
-    const int n_val = rows * M, nv = (n_val + 31) >> 5;  // values per lane: e = lane + 32 j
-    float v[16];
+  // Only a warp's first unit can be one it finishes: its last unit, when cut,
+  // continues in a higher warp. The finishing (highest) warp of a cut unit
+  // adds the partials in warp order and writes y.
+  const int u_start = cut_s0, u_end = cut_s0 + n_chunks;
+  const bool own = cut_t0 >= 0 && begin_of(wg + 1) >= u_end;  // units never cross a cluster boundary
+  float v[16];
 #pragma unroll
-    for (int j = 0; j < 16; ++j) v[j] = 0.0f;
-    // eight warps' partials at a time: their loads are issued together and
-    // added in warp order afterwards
+  for (int j = 0; j < 16; ++j) v[j] = 0.0f;
+  int nv = 0, n_val = 0, rows = 0;
+  if (own) {
+    rows = P.w[cut_t0].mt * kTileRows;
+    n_val = rows * M;
+    nv = (n_val + 31) >> 5;  // values per lane: e = lane + 32 j
     // first warp holding part of the unit: the last of the cluster with begin <= u_start
     const int w_first = cl_base + 31 - __clz(__ballot_sync(0xffffffffu, b_lane <= u_start));
+    // eight warps' partials at a time: their loads are issued together and
+    // added in warp order afterwards
     for (int w0 = w_first; w0 <= wg; w0 += 8) {
       uint32_t src[8];
       bool ok[8];
@@ -818,6 +823,17 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kThreads, 1)
           if (ok[q]) v[j] += a[q];
       }
     }
+  }
+  // This warp reads no more of the peer's shared memory: arrive now and wait
+  // only before leaving, so the stores below overlap the barrier. The sum of
+  // the partials is an operand of the arrive, which keeps every load before it.
+  float dep = 0.0f;
+#pragma unroll
+  for (int j = 0; j < 16; ++j) dep += v[j];
+  cluster_arrive_after(dep);
+  if (own) {
+    const int unit = cut_u0;
+    const csaq_tier& T = P.tp.t[cut_t0];
 #pragma unroll
     for (int j = 0; j < 16; ++j) {
       if (j >= nv) break;
@@ -825,7 +841,7 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kThreads, 1)
       if (e < n_val && row < T.n_rows) store_out<ACT>(T, row, tok, v[j], xexp[tok]);
     }
   }
-  cluster_sync();  // no CTA leaves while the other may still read its partials
+  cluster_wait();  // no CTA leaves while the other may still read its partials
 }
 
 // ── CUDA-core reference kernel ──────────────────────────────────────────────
