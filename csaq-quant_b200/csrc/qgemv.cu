@@ -321,8 +321,37 @@ __device__ __forceinline__ int tier_of_item(const KParams& P, int item) {
   return t;
 }
 
-template <typename ACT>
-__device__ __forceinline__ void store_out(const csaq_tier& T, int row, int tok, float v, float xe) {
+// a value the compiler must have in a register at this point of the program
+// (so a load is issued here, not sunk past the barriers that follow)
+template <typename V>
+__device__ __forceinline__ V pin(V v) {
+  static_assert(sizeof(V) == 4 || sizeof(V) == 8, "pin: 4 or 8 bytes");
+  if constexpr (sizeof(V) == 8) {
+    uint64_t u;
+    memcpy(&u, &v, 8);
+    asm volatile("mov.b64 %0, %0;" : "+l"(u));
+    memcpy(&v, &u, 8);
+  } else {
+    uint32_t u;
+    memcpy(&u, &v, 4);
+    asm volatile("mov.b32 %0, %0;" : "+r"(u));
+    memcpy(&v, &u, 4);
+  }
+  return v;
+}
+
+// the fields of a tier that writing y needs
+struct OutDesc {
+  const int32_t* out_rows;
+  const void* bias;
+  const void* residual;
+  void* y;
+  int64_t ldy, ldr;
+  int n_rows;
+};
+
+template <typename ACT, typename TD>
+__device__ __forceinline__ void store_out(const TD& T, int row, int tok, float v, float xe) {
   v = __fmul_rn(v, xe);
   const int orow = T.out_rows[row];
   if (T.bias) v = __fadd_rn(v, to_f32<ACT>(reinterpret_cast<const ACT*>(T.bias)[orow]));
@@ -743,6 +772,22 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kThreads, 1)
       do { ++t; } while (item < it_end && P.w[t].n_items == 0);
     }
   }
+  // What the tail needs from the kernel parameters, read now (loads with a
+  // warp-dependent index miss the constant cache; their latency overlaps the
+  // barriers below instead of following them): the cluster's range starts
+  // and the output description of the warp's first unit.
+  const int cl_base = wg - (wg & 31);
+  const int b_lane = pin(P.begin[cl_base + lane]), b_end = pin(P.begin[cl_base + 32]);
+  const int t_own = cut_t0 >= 0 ? cut_t0 : 0;
+  const int own_rows = pin(P.w[t_own].mt) * kTileRows;
+  OutDesc od;
+  od.out_rows = pin(P.tp.t[t_own].out_rows);
+  od.bias = pin(P.tp.t[t_own].bias);
+  od.residual = pin(P.tp.t[t_own].residual);
+  od.y = pin(P.tp.t[t_own].y);
+  od.ldy = pin(P.tp.t[t_own].ldy);
+  od.ldr = pin(P.tp.t[t_own].ldr);
+  od.n_rows = pin(P.tp.t[t_own].n_rows);
   if (late) {
     if (lane == 0) atomicAdd(&g_wait_timeouts, 1u);
     // let the abandoned copies land (again bounded) before shared memory is reused
@@ -776,8 +821,6 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kThreads, 1)
   // cl_base + l's (kernel-parameter loads with a varying index are slow):
   // begin[w] of any warp of the cluster is one shuffle away
   static_assert(kWarps * kCluster == 32, "one lane per warp of a cluster");
-  const int cl_base = wg - (wg & 31);
-  const int b_lane = P.begin[cl_base + lane], b_end = P.begin[cl_base + 32];
   auto begin_of = [&](int w) {  // w in [cl_base, cl_base + 32]
     const int v = __shfl_sync(0xffffffffu, b_lane, (w - cl_base) & 31);
     return w - cl_base == 32 ? b_end : v;
@@ -792,7 +835,7 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kThreads, 1)
   for (int j = 0; j < 16; ++j) v[j] = 0.0f;
   int nv = 0, n_val = 0, rows = 0;
   if (own) {
-    rows = P.w[cut_t0].mt * kTileRows;
+    rows = own_rows;
     n_val = rows * M;
     nv = (n_val + 31) >> 5;  // values per lane: e = lane + 32 j
     // first warp holding part of the unit: the last of the cluster with begin <= u_start
@@ -833,12 +876,11 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kThreads, 1)
   cluster_arrive_after(dep);
   if (own) {
     const int unit = cut_u0;
-    const csaq_tier& T = P.tp.t[cut_t0];
 #pragma unroll
     for (int j = 0; j < 16; ++j) {
       if (j >= nv) break;
       const int e = lane + 32 * j, r = e / M, tok = e - r * M, row = unit * rows + r;
-      if (e < n_val && row < T.n_rows) store_out<ACT>(T, row, tok, v[j], xexp[tok]);
+      if (e < n_val && row < od.n_rows) store_out<ACT>(od, row, tok, v[j], xexp[tok]);
     }
   }
   cluster_wait();  // no CTA leaves while the other may still read its partials
