@@ -605,24 +605,34 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kThreads, 1)
   // issue cursor: walks the warp's items (consecutive blocks of each tier)
   int i_left = it_end - it_begin, i_local = 0;
   int i_t = 0, i_slot = 0;
+  // the current tier's fields, reloaded from the kernel parameters only when
+  // the cursor enters another tier (indexed parameter loads miss the constant cache)
+  const uint8_t* i_blocks = nullptr;
+  int i_cb = 0, i_n = 0;
+  auto enter_tier = [&]() {
+    i_blocks = P.tp.t[i_t].blocks;
+    i_cb = chunk_bytes(P.w[i_t].bits);
+    i_n = P.w[i_t].n_items;
+  };
+  const int slot_bytes = P.slot_bytes, depth = P.depth;
   if (i_left > 0) {
     i_t = tier_of_item(P, it_begin);
     i_local = it_begin - P.w[i_t].item0;
+    enter_tier();
   }
   auto issue = [&]() {
     if (i_left > 0) {
       if (lane == 0) {
-        const int cb = chunk_bytes(P.w[i_t].bits);
-        mbar_expect_tx(&bars[i_slot], (uint32_t)cb);
-        bulk_load(ring + i_slot * P.slot_bytes, P.tp.t[i_t].blocks + (int64_t)i_local * cb, (uint32_t)cb,
-                  &bars[i_slot]);
+        mbar_expect_tx(&bars[i_slot], (uint32_t)i_cb);
+        bulk_load(ring + i_slot * slot_bytes, i_blocks + (int64_t)i_local * i_cb, (uint32_t)i_cb, &bars[i_slot]);
       }
       --i_left;
-      if (++i_local == P.w[i_t].n_items) {
+      if (++i_local == i_n) {
         i_local = 0;
         do { ++i_t; } while (i_left > 0 && P.w[i_t].n_items == 0);
+        if (i_left > 0) enter_tier();
       }
-      i_slot = (i_slot + 1 == P.depth) ? 0 : i_slot + 1;
+      i_slot = (i_slot + 1 == depth) ? 0 : i_slot + 1;
     }
   };
   for (int d = 0; d < P.depth; ++d) issue();  // weights first: no kernel writes them
