@@ -733,9 +733,16 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kThreads, 1)
       c_slot = (c_slot + 1 == P.depth) ? 0 : c_slot + 1;
     }
   };
+  // the current tier's work fields, reloaded only at tier boundaries
+  int c_bits = 0, c_mt = 0, c_item0 = 0, c_n = 0;
+  auto enter_ctier = [&]() {
+    c_bits = P.w[t].bits;
+    c_mt = P.w[t].mt;
+    c_item0 = P.w[t].item0;
+    c_n = P.w[t].n_items;
+  };
+  if (item < it_end) enter_ctier();
   while (item < it_end) {
-    const TierWork& tw = P.w[t];
-    const csaq_tier& T = P.tp.t[t];
     const int unit = local / n_chunks;
     const int ch_first = local - unit * n_chunks;
     const int room = it_end - item;
@@ -744,24 +751,25 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kThreads, 1)
     for (int a = 0; a < 2; ++a)
 #pragma unroll
       for (int nt = 0; nt < NT; ++nt) acc[a][nt][0] = acc[a][nt][1] = acc[a][nt][2] = acc[a][nt][3] = 0.0f;
-    switch (tw.bits) {
+    switch (c_bits) {
       case 4: chunks(std::integral_constant<int, 4>(), ch_first, ch_last); break;
       case 8: chunks(std::integral_constant<int, 8>(), ch_first, ch_last); break;
       case 16: chunks(std::integral_constant<int, 16>(), ch_first, ch_last); break;
       default: chunks(std::integral_constant<int, 2>(), ch_first, ch_last); break;
     }
 
-    const int u_start = tw.item0 + unit * n_chunks;
+    const int u_start = c_item0 + unit * n_chunks;
     if (ch_first == 0 && ch_last == n_chunks) {
       // the whole unit is in this warp: write y from the fragments
+      const csaq_tier& T = P.tp.t[t];
 #pragma unroll
       for (int mt = 0; mt < 2; ++mt)
 #pragma unroll
         for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
           for (int e = 0; e < 4; ++e) {
-            const int row = unit * tw.mt * kTileRows + frag_row(mt, e, lane), tok = frag_tok(nt, e, lane);
-            if (mt < tw.mt && tok < M && row < T.n_rows) store_out<ACT>(T, row, tok, acc[mt][nt][e], xexp[tok]);
+            const int row = unit * c_mt * kTileRows + frag_row(mt, e, lane), tok = frag_tok(nt, e, lane);
+            if (mt < c_mt && tok < M && row < T.n_rows) store_out<ACT>(T, row, tok, acc[mt][nt][e], xexp[tok]);
           }
     } else if (item == it_begin) {
       cut_t0 = t; cut_u0 = unit; cut_s0 = u_start;
@@ -777,9 +785,10 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kThreads, 1)
 
     item += ch_last - ch_first;
     local += ch_last - ch_first;
-    if (local == tw.n_items) {
+    if (local == c_n) {
       local = 0;
       do { ++t; } while (item < it_end && P.w[t].n_items == 0);
+      if (item < it_end) enter_ctier();
     }
   }
   // What the tail needs from the kernel parameters, read now (loads with a
