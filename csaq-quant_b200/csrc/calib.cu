@@ -48,6 +48,60 @@ __global__ void mask_kernel(const T* __restrict__ act, int64_t n_tok, int64_t C,
   bits[c * ld_bits + word_off + w] = word;
 }
 
+// The same masks from 16-byte loads: a thread reads V = 16/sizeof(T)
+// channels of one token per load (a warp reads 512 contiguous bytes of a
+// token row) and builds V words of 32 tokens; a CTA covers 32*V channels x
+// 256 tokens and writes each channel's 8 words (32 contiguous bytes) through
+// shared memory, so the bit stores are whole sectors. Needs C and ld to be
+// multiples of V and a 16-byte aligned act.
+template <typename T>
+__global__ void __launch_bounds__(256) mask_vec_kernel(const T* __restrict__ act, int64_t n_tok, int64_t C,
+                                                       int64_t ld, int mode, float thr,
+                                                       const uint32_t* __restrict__ tok_thr,
+                                                       uint32_t* __restrict__ bits, int64_t ld_bits,
+                                                       int64_t word_off) {
+  constexpr int V = 16 / sizeof(T);
+  constexpr int CH = 32 * V;
+  constexpr uint32_t MAG = sizeof(T) == 2 ? 0x7FFFu : 0x7FFFFFFFu;
+  __shared__ uint32_t tile[CH][9];
+  const int g = threadIdx.x & 31, wy = threadIdx.x >> 5;
+  const int64_t c0 = int64_t(blockIdx.x) * CH;
+  const int64_t cg = c0 + g * V;
+  const int64_t t0 = (int64_t(blockIdx.y) * 8 + wy) * 32;
+  uint32_t word[V];
+#pragma unroll
+  for (int q = 0; q < V; ++q) word[q] = 0u;
+  auto take = [&](int b, const uint4& v) {
+    const T* e = reinterpret_cast<const T*>(&v);
+    const uint32_t tt = mode == 1 ? __ldg(tok_thr + t0 + b) : 0u;
+#pragma unroll
+    for (int q = 0; q < V; ++q) {
+      const bool on = mode == 0 ? to_f32<T>(e[q]) > thr : (bits_of<T>(e[q]) & MAG) >= tt;
+      word[q] |= (uint32_t)on << b;
+    }
+  };
+  if (cg < C && t0 < n_tok) {
+    const uint4* src = reinterpret_cast<const uint4*>(act + t0 * ld + cg);
+    const int64_t step = ld / V;  // one token row, in 16-byte units
+    const int64_t left = n_tok - t0;
+    if (left >= 32) {
+#pragma unroll 8
+      for (int b = 0; b < 32; ++b) take(b, __ldcs(src + b * step));
+    } else {
+      for (int b = 0; b < (int)left; ++b) take(b, __ldcs(src + b * step));
+    }
+  }
+#pragma unroll
+  for (int q = 0; q < V; ++q) tile[g * V + q][wy] = word[q];
+  __syncthreads();
+  const int64_t n_words = (n_tok + 31) / 32;
+  for (int e = threadIdx.x; e < CH * 8; e += blockDim.x) {
+    const int ch = e >> 3, ww = e & 7;
+    const int64_t c = c0 + ch, w = int64_t(blockIdx.y) * 8 + ww;
+    if (c < C && w < n_words) bits[c * ld_bits + word_off + w] = tile[ch][ww];
+  }
+}
+
 // Per-token k-th largest |o| by radix select on magnitude bit patterns
 // (16-bit types: 2 passes of 8 bits; fp32: 4 passes). One CTA per token.
 template <typename T>
@@ -166,59 +220,130 @@ __global__ void popc_rows_kernel(const uint32_t* __restrict__ bits, int64_t C, i
 
 // J = I / max(f_i + f_j - I, 1) in fp32 (csaq/core.py:263-265) and the bit
 // J >= thr (thr already rounded to fp32, as torch compares a float32 tensor
-// with a Python float). One warp per 32 columns of one row: ballot -> word.
+// with a Python float). One warp per 8 words (256 columns) of one row: eight
+// independent coalesced loads per lane, one ballot per word.
 __global__ void jaccard_bits_kernel(const int32_t* __restrict__ inter, int64_t ld_i,
                                     const int32_t* __restrict__ f, int64_t C, float thr,
                                     uint32_t* __restrict__ adj, int64_t ld_adj) {
   const int64_t gw = (int64_t(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   const int64_t words_per_row = (C + 31) / 32;
-  if (gw >= C * words_per_row) return;
-  const int64_t i = gw / words_per_row, w = gw % words_per_row;
-  const int64_t j = w * 32 + lane;
-  bool on = false;
-  if (j < C) {
-    const float I = (float)inter[i * ld_i + j];
-    const float uni = fmaxf(__fsub_rn(__fadd_rn((float)f[i], (float)f[j]), I), 1.0f);
-    on = __fdiv_rn(I, uni) >= thr;
+  const int64_t groups = (words_per_row + 7) / 8;
+  if (gw >= C * groups) return;  // whole warps
+  const int64_t i = gw / groups, w0 = (gw % groups) * 8;
+  const float fi = (float)__ldg(f + i);
+  const int32_t* row = inter + i * ld_i;
+  int32_t v[8], fj[8];
+#pragma unroll
+  for (int k = 0; k < 8; ++k) {
+    const int64_t j = (w0 + k) * 32 + lane;
+    v[k] = j < C ? __ldcs(row + j) : 0;
+    fj[k] = j < C ? __ldg(f + j) : 0;
   }
-  const uint32_t word = __ballot_sync(0xffffffffu, on);
-  if (lane == 0) adj[i * ld_adj + w] = word;
+  uint32_t mine = 0u;
+#pragma unroll
+  for (int k = 0; k < 8; ++k) {
+    const int64_t j = (w0 + k) * 32 + lane;
+    bool on = false;
+    if (j < C) {
+      const float I = (float)v[k];
+      const float uni = fmaxf(__fsub_rn(__fadd_rn(fi, (float)fj[k]), I), 1.0f);
+      on = __fdiv_rn(I, uni) >= thr;
+    }
+    const uint32_t word = __ballot_sync(0xffffffffu, on);
+    if (lane == k) mine = word;
+  }
+  if (lane < 8 && w0 + lane < words_per_row) adj[i * ld_adj + w0 + lane] = mine;
 }
 
-// Seed-order greedy partition (csaq/core.py:268-285), one CTA. Channels j < i
-// are always visited when seed i is reached, so clique(i) = {i} + {j > i :
-// adj[i][j] and not visited}. labels[c] = index of c's clique in seed order.
-__global__ void __launch_bounds__(1024) greedy_kernel(const uint32_t* __restrict__ adj,
-                                                      int64_t ld_adj, int C,
-                                                      int32_t* __restrict__ labels,
-                                                      int32_t* __restrict__ n_cliques) {
-  extern __shared__ uint32_t visited[];
-  const int words = (C + 31) / 32;
-  for (int w = threadIdx.x; w < words; w += blockDim.x) visited[w] = 0u;
-  __syncthreads();
-  int id = 0;
-  for (int i = 0; i < C; ++i) {
-    if (visited[i >> 5] & (1u << (i & 31))) continue;  // uniform across the block
-    __syncthreads();
-    const uint32_t* row = adj + (int64_t)i * ld_adj;
-    for (int w = threadIdx.x; w < words; w += blockDim.x) {
-      uint32_t m = row[w] & ~visited[w];
-      if (w == (i >> 5)) m |= 1u << (i & 31);
-      if (w < (i >> 5)) m = 0u;
-      if (m) {
-        visited[w] |= m;
-        while (m) {
-          const int b = __ffs(m) - 1;
-          m &= m - 1;
-          labels[(int64_t)w * 32 + b] = id;
-        }
-      }
-    }
-    ++id;
-    __syncthreads();
+// Seed-order greedy partition (csaq/core.py:268-285). Channels j < i are
+// always taken when seed i is reached, so clique(i) = {i} + {j > i : adj[i][j]
+// and j not taken}; labels[c] = index of c's clique in seed order. Bits of
+// columns >= C are ignored.
+//
+// Pass 1 (row_tail_kernel, parallel): flag[i] = row i has a bit above the
+// diagonal, i.e. seed i may take members. The flags are written into labels,
+// which pass 2 overwrites.
+// Pass 2 (greedy_seq_kernel, one warp): walks the seeds 32 at a time (one word
+// of channels). The taken bits of the current word live in a register; a
+// seed without a flag costs a few register operations, and only flagged
+// seeds read their row (L2-resident after pass 1) and update the taken set of
+// later words in shared memory. Labels of the current word's channels are
+// kept one per lane and stored once per word; members in later words are
+// labelled directly, and their flag slots are not read again (they are taken).
+__global__ void row_tail_kernel(const uint32_t* __restrict__ adj, int64_t ld_adj, int64_t C,
+                                int32_t* __restrict__ flag) {
+  const int64_t i = (int64_t(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (i >= C) return;  // whole warps
+  const int64_t words = (C + 31) / 32, w0 = i >> 5;
+  const uint32_t last = (C & 31) ? (1u << (C & 31)) - 1u : 0xffffffffu;
+  const uint32_t* row = adj + i * ld_adj;
+  uint32_t any = 0u;
+  for (int64_t w = w0 + lane; w < words; w += 32) {
+    uint32_t v = row[w];
+    if (w == w0) v &= ~((2u << (i & 31)) - 1u);
+    if (w == words - 1) v &= last;
+    any |= v;
   }
-  if (threadIdx.x == 0) *n_cliques = id;
+  any = __any_sync(0xffffffffu, any != 0u);
+  if (lane == 0) flag[i] = any ? 1 : 0;
+}
+
+__global__ void __launch_bounds__(32) greedy_seq_kernel(const uint32_t* __restrict__ adj, int64_t ld_adj, int C,
+                                                        int32_t* labels, int32_t* __restrict__ n_cliques) {
+  extern __shared__ uint32_t taken_s[];  // taken channels, one bit each
+  const int lane = threadIdx.x;
+  const int words = (C + 31) / 32;
+  const uint32_t last = (C & 31) ? (1u << (C & 31)) - 1u : 0xffffffffu;
+  for (int w = lane; w < words; w += 32) taken_s[w] = 0u;
+  __syncwarp();
+  int id = 0;
+  int next_flag = lane < C ? labels[lane] : 0;
+  for (int w0 = 0; w0 < words; ++w0) {
+    const int i0 = w0 * 32;
+    const int flag = next_flag;
+    next_flag = i0 + 32 + lane < C ? labels[i0 + 32 + lane] : 0;  // in flight while this word runs
+    uint32_t tw = taken_s[w0];  // uniform across the warp from here on
+    const uint32_t taken0 = tw;
+    const uint32_t flagged = __ballot_sync(0xffffffffu, flag != 0);
+    const int nb = C - i0 < 32 ? C - i0 : 32;
+    int my = 0;
+    for (int b = 0; b < nb; ++b) {
+      if (tw & (1u << b)) continue;
+      tw |= 1u << b;
+      if (lane == b) my = id;
+      if (flagged & (1u << b)) {
+        const uint32_t* row = adj + (int64_t)(i0 + b) * ld_adj;
+        const uint32_t r0 = row[w0];
+        int w = w0 + 1 + lane;
+        uint32_t r = w < words ? row[w] : 0u;
+        uint32_t m0 = r0 & ~tw & ~((2u << b) - 1u);
+        if (w0 == words - 1) m0 &= last;
+        tw |= m0;
+        if ((m0 >> lane) & 1u) my = id;
+        for (; w < words; w += 32) {
+          const uint32_t rn = w + 32 < words ? row[w + 32] : 0u;
+          uint32_t m = r & ~taken_s[w];
+          if (w == words - 1) m &= last;
+          if (m) {
+            taken_s[w] |= m;
+            do {
+              const int bb = __ffs(m) - 1;
+              m &= m - 1;
+              labels[w * 32 + bb] = id;
+            } while (m);
+          }
+          r = rn;
+        }
+        __syncwarp();
+      }
+      ++id;
+    }
+    if (lane < nb && !((taken0 >> lane) & 1u)) labels[i0 + lane] = my;
+    __syncwarp();
+  }
+  if (lane == 0) *n_cliques = id;
 }
 
 // ── salience: acc += |G * W| in fp32 (csaq/core.py:204-210) ────────────────
@@ -305,8 +430,20 @@ extern "C" int csaq_act_mask(const void* act, int dtype, int64_t n_tok, int64_t 
       if (rc) return rc;
     }
   }
-  const dim3 grid((unsigned)((C + kThreads - 1) / kThreads), (unsigned)((n_tok + 31) / 32));
   const int64_t woff = tok_offset / 32;
+  const int64_t n_words = (n_tok + 31) / 32;
+  const int V = 16 / (int)dtype_size(dtype);
+  if (C % V == 0 && ld % V == 0 && reinterpret_cast<uintptr_t>(act) % 16 == 0 && (n_words + 7) / 8 <= 65535) {
+    const dim3 vgrid((unsigned)((C + 32 * V - 1) / (32 * V)), (unsigned)((n_words + 7) / 8));
+    switch (dtype) {
+      case CSAQ_DT_F32: mask_vec_kernel<float><<<vgrid, 256, 0, st>>>(reinterpret_cast<const float*>(act), n_tok, C, ld, mode, thr, tok_thr, bits, ld_bits, woff); break;
+      case CSAQ_DT_F16: mask_vec_kernel<__half><<<vgrid, 256, 0, st>>>(reinterpret_cast<const __half*>(act), n_tok, C, ld, mode, thr, tok_thr, bits, ld_bits, woff); break;
+      default: mask_vec_kernel<__nv_bfloat16><<<vgrid, 256, 0, st>>>(reinterpret_cast<const __nv_bfloat16*>(act), n_tok, C, ld, mode, thr, tok_thr, bits, ld_bits, woff); break;
+    }
+    return launch_status();
+  }
+  if (n_words > 65535) return CSAQ_ERR_UNSUPPORTED;
+  const dim3 grid((unsigned)((C + kThreads - 1) / kThreads), (unsigned)n_words);
   switch (dtype) {
     case CSAQ_DT_F32: mask_kernel<float><<<grid, kThreads, 0, st>>>(reinterpret_cast<const float*>(act), n_tok, C, ld, mode, thr, tok_thr, bits, ld_bits, woff); break;
     case CSAQ_DT_F16: mask_kernel<__half><<<grid, kThreads, 0, st>>>(reinterpret_cast<const __half*>(act), n_tok, C, ld, mode, thr, tok_thr, bits, ld_bits, woff); break;
@@ -331,7 +468,7 @@ extern "C" int csaq_coact_counts(const uint32_t* bits, int64_t C, int64_t n_word
 extern "C" int csaq_jaccard_bits(const int32_t* inter, int64_t ld_i, const int32_t* f, int64_t C,
                                  float threshold, uint32_t* adj, int64_t ld_adj, void* stream) {
   if (!inter || !f || !adj || C <= 0 || ld_i < C || ld_adj < (C + 31) / 32) return CSAQ_ERR_ARG;
-  const int64_t warps = C * ((C + 31) / 32);
+  const int64_t warps = C * (((C + 31) / 32 + 7) / 8);
   jaccard_bits_kernel<<<blocks_for(warps * 32), kThreads, 0, as_stream(stream)>>>(
       inter, ld_i, f, C, threshold, adj, ld_adj);
   return launch_status();
@@ -341,13 +478,18 @@ extern "C" int csaq_greedy_cliques(const uint32_t* adj, int64_t ld_adj, int64_t 
                                    int32_t* n_cliques, void* stream) {
   if (!adj || !labels || !n_cliques || C <= 0 || ld_adj < (C + 31) / 32) return CSAQ_ERR_ARG;
   const int64_t words = (C + 31) / 32;
-  if (words * 4 > 200 * 1024) return CSAQ_ERR_UNSUPPORTED;  // visited set lives in shared memory
+  if (words * 4 > 200 * 1024) return CSAQ_ERR_UNSUPPORTED;  // the taken set lives in shared memory
+  cudaStream_t st = as_stream(stream);
+  row_tail_kernel<<<blocks_for(C * 32), kThreads, 0, st>>>(adj, ld_adj, C, labels);
+  int rc = launch_status();
+  if (rc) return rc;
   const size_t smem = (size_t)words * 4;
   if (smem > 48 * 1024) {
-    if (cudaFuncSetAttribute(greedy_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
+    if (cudaFuncSetAttribute(greedy_seq_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
+        cudaSuccess)
       return launch_status();
   }
-  greedy_kernel<<<1, 1024, smem, as_stream(stream)>>>(adj, ld_adj, (int)C, labels, n_cliques);
+  greedy_seq_kernel<<<1, 32, smem, st>>>(adj, ld_adj, (int)C, labels, n_cliques);
   return launch_status();
 }
 

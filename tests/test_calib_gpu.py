@@ -129,6 +129,44 @@ def test_full_size_coactivation_digest(digests):
         assert _sha(_labels(cl, 11008)) == d[f"labels_{thr}"], thr
 
 
+def _greedy_ref(rows, C):
+    """Seed-order partition (csaq/core.py:268-285) over sparse adjacency rows:
+    seed i takes itself and every unvisited j > i of its row."""
+    visited = np.zeros(C, bool)
+    lab = np.empty(C, np.int32)
+    nid = 0
+    for i in range(C):
+        if visited[i]:
+            continue
+        mem = [j for j in rows[i] if j > i and not visited[j]] + [i]
+        visited[mem] = True
+        lab[mem] = nid
+        nid += 1
+    return lab, nid
+
+
+@pytest.mark.parametrize("C,ld_pad,per_row", [(3000, 3, 6), (33, 0, 20), (40000, 0, 3)])
+def test_greedy_cliques_on_arbitrary_adjacency(C, ld_pad, per_row):
+    """csaq_greedy_cliques on random (asymmetric) adjacency bits, including a
+    padded row stride and rows wider than one CTA (C > 32768)."""
+    from csaq._lib import check, lib
+    rng = np.random.default_rng(C)
+    words = (C + 31) // 32
+    ld = words + ld_pad
+    rows = [np.unique(rng.integers(0, C, size=per_row)) for _ in range(C)]
+    adj = np.zeros((C, ld), np.uint32)
+    for i, r in enumerate(rows):
+        np.bitwise_or.at(adj[i], r // 32, (np.uint32(1) << (r % 32).astype(np.uint32)))
+    a = torch.from_numpy(adj.view(np.int32)).to(DEV)
+    labels = torch.full((C,), -7, dtype=torch.int32, device=DEV)
+    n = torch.zeros(1, dtype=torch.int32, device=DEV)
+    check(lib().csaq_greedy_cliques(a.data_ptr(), ld, C, labels.data_ptr(), n.data_ptr(),
+                                    torch.cuda.current_stream().cuda_stream), "greedy")
+    ref, nid = _greedy_ref(rows, C)
+    assert int(n.item()) == nid
+    np.testing.assert_array_equal(labels.cpu().numpy(), ref)
+
+
 def test_profile_end_to_end_tiny_decoder():
     """CausalProfiler.profile on a tiny Llama: salience is |G W| averaged over
     batches (checked against torch on the same grads) and cliques partition
