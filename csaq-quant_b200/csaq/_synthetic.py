@@ -100,11 +100,12 @@ DECODERS = {
     "llama3-70b": ("llama", 8192, 28672, 80, 64, 8, 128256),
     "tiny-llama": ("llama", 512, 1536, 2, 4, 2, 2048),
     "tiny-qwen2": ("qwen2", 512, 1408, 2, 4, 4, 2048),
+    "tiny-qwen2-d64": ("qwen2", 256, 768, 2, 4, 4, 2048),  # 64-wide heads, like Qwen1.5-0.5B
 }
 
 
 def decoder_config(name: str, n_layers: int = None):
-    """HF config of a decoder shape (head_dim 128, default rope)."""
+    """HF config of a decoder shape (head_dim hidden/heads: 64 or 128; default rope)."""
     from transformers import LlamaConfig, Qwen2Config
     arch, h, inter, layers, heads, kv, vocab = DECODERS[name]
     kw = dict(hidden_size=h, intermediate_size=inter, num_hidden_layers=n_layers or layers,

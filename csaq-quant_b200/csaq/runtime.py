@@ -57,7 +57,8 @@ def _layers_of(model: nn.Module):
 
 
 def supports(model: nn.Module) -> bool:
-    """True for Llama/Qwen2-style decoders whose attention/MLP linears are CSAQLinear."""
+    """True for Llama/Qwen2-style decoders whose attention/MLP linears are
+    CSAQLinear, with 64- or 128-wide heads (the decode attention kernel's)."""
     inner, layers = _layers_of(model)
     if layers is None or len(layers) == 0:
         return False
@@ -72,7 +73,7 @@ def supports(model: nn.Module) -> bool:
         return False
     cfg = getattr(model, "config", None)
     head_dim = getattr(cfg, "head_dim", None) or (cfg.hidden_size // cfg.num_attention_heads)
-    return head_dim == 128 and getattr(model, "lm_head", None) is not None
+    return head_dim in (64, 128) and getattr(model, "lm_head", None) is not None
 
 
 @dataclass

@@ -193,12 +193,12 @@ __device__ __forceinline__ void cp_async_commit_wait_all() {
 constexpr int kChunk = 64;
 constexpr int kAttnWarps = 4;
 
-template <typename T>
+template <typename T, int D>
 __global__ void __launch_bounds__(kAttnWarps * 32) attention_kernel(
     const T* __restrict__ q, const T* __restrict__ k_cache, const T* __restrict__ v_cache,
     const int32_t* __restrict__ pos0, int S, int Hq, int Hkv, int Lmax, float scale,
     float* __restrict__ part, int32_t* __restrict__ tickets, T* __restrict__ out) {
-  constexpr int D = 128;
+  constexpr int E = D / 32;  // head elements per lane
   const int bh = blockIdx.x, sp = blockIdx.y, n_split = gridDim.y;
   const int b = bh / Hkv, h = bh % Hkv;
   const int G = Hq / Hkv, R = S * G;
@@ -235,11 +235,13 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attention_kernel(
     const int s = r / G, hq = h * G + r % G;
     const int qpos = pos0[b] + s;  // attends keys 0..qpos
     const T* qr = q + (((int64_t)b * S + s) * Hq + hq) * D;
-    float qv[4];
+    float qv[E];
 #pragma unroll
-    for (int i = 0; i < 4; ++i) qv[i] = to_f32<T>(qr[lane * 4 + i]) * scale;
+    for (int i = 0; i < E; ++i) qv[i] = to_f32<T>(qr[lane * E + i]) * scale;
     const int kmax = min(n_keys, qpos - k0 + 1);
-    float m = -INFINITY, l = 0.0f, o[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+    float m = -INFINITY, l = 0.0f, o[E];
+#pragma unroll
+    for (int i = 0; i < E; ++i) o[i] = 0.0f;
     int j = 0;
     for (; j + 4 <= kmax; j += 4) {  // four keys per step: independent dot products
       float d[4];
@@ -247,7 +249,7 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attention_kernel(
       for (int t = 0; t < 4; ++t) {
         d[t] = 0.0f;
 #pragma unroll
-        for (int i = 0; i < 4; ++i) d[t] = fmaf(qv[i], to_f32<T>(ks[j + t][lane * 4 + i]), d[t]);
+        for (int i = 0; i < E; ++i) d[t] = fmaf(qv[i], to_f32<T>(ks[j + t][lane * E + i]), d[t]);
       }
 #pragma unroll
       for (int off = 16; off > 0; off >>= 1)
@@ -260,10 +262,10 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attention_kernel(
       for (int t = 0; t < 4; ++t) p[t] = __expf(d[t] - mn);
       l = fmaf(l, corr, (p[0] + p[1]) + (p[2] + p[3]));
 #pragma unroll
-      for (int i = 0; i < 4; ++i) {
+      for (int i = 0; i < E; ++i) {
         float acc = o[i] * corr;
 #pragma unroll
-        for (int t = 0; t < 4; ++t) acc = fmaf(p[t], to_f32<T>(vs[j + t][lane * 4 + i]), acc);
+        for (int t = 0; t < 4; ++t) acc = fmaf(p[t], to_f32<T>(vs[j + t][lane * E + i]), acc);
         o[i] = acc;
       }
       m = mn;
@@ -271,19 +273,19 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attention_kernel(
     for (; j < kmax; ++j) {
       float d = 0.0f;
 #pragma unroll
-      for (int i = 0; i < 4; ++i) d = fmaf(qv[i], to_f32<T>(ks[j][lane * 4 + i]), d);
+      for (int i = 0; i < E; ++i) d = fmaf(qv[i], to_f32<T>(ks[j][lane * E + i]), d);
 #pragma unroll
       for (int off = 16; off > 0; off >>= 1) d += __shfl_xor_sync(0xffffffffu, d, off);
       const float mn = fmaxf(m, d);
       const float corr = __expf(m - mn), p = __expf(d - mn);
       l = l * corr + p;
 #pragma unroll
-      for (int i = 0; i < 4; ++i) o[i] = fmaf(o[i], corr, p * to_f32<T>(vs[j][lane * 4 + i]));
+      for (int i = 0; i < E; ++i) o[i] = fmaf(o[i], corr, p * to_f32<T>(vs[j][lane * E + i]));
       m = mn;
     }
     float* pr = pbase + (int64_t)r * (D + 2);
 #pragma unroll
-    for (int i = 0; i < 4; ++i) pr[lane * 4 + i] = o[i];
+    for (int i = 0; i < E; ++i) pr[lane * E + i] = o[i];
     if (lane == 0) { pr[D] = m; pr[D + 1] = l; }
   }
   __threadfence();
@@ -299,7 +301,9 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attention_kernel(
 #pragma unroll 8
     for (int p = 0; p < n_split; ++p)
       M_ = fmaxf(M_, __ldcg(part + (((int64_t)bh * n_split + p) * R + r) * (D + 2) + D));
-    float L = 0.0f, o[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+    float L = 0.0f, o[E];
+#pragma unroll
+    for (int i = 0; i < E; ++i) o[i] = 0.0f;
 #pragma unroll 4
     for (int p = 0; p < n_split; ++p) {
       const float* pr = part + (((int64_t)bh * n_split + p) * R + r) * (D + 2);
@@ -308,12 +312,12 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attention_kernel(
       const float w = __expf(mp - M_);
       L = fmaf(__ldcg(pr + D + 1), w, L);
 #pragma unroll
-      for (int i = 0; i < 4; ++i) o[i] = fmaf(__ldcg(pr + lane * 4 + i), w, o[i]);
+      for (int i = 0; i < E; ++i) o[i] = fmaf(__ldcg(pr + lane * E + i), w, o[i]);
     }
     T* orow = out + (((int64_t)b * S + s) * Hq + hq) * D;
     const float inv = L > 0.0f ? 1.0f / L : 0.0f;
 #pragma unroll
-    for (int i = 0; i < 4; ++i) orow[lane * 4 + i] = from_f32<T>(o[i] * inv);
+    for (int i = 0; i < E; ++i) orow[lane * E + i] = from_f32<T>(o[i] * inv);
   }
   if (threadIdx.x == 0) tickets[bh] = 0;
 }
@@ -529,20 +533,30 @@ extern "C" int64_t csaq_attention_workspace_floats(int64_t B, int64_t S, int64_t
   return B * Hkv * n_split * S * (Hq / Hkv) * (D + 2);
 }
 
+template <typename T>
+static int launch_attention(int64_t D, dim3 grid, cudaStream_t st, const void* q, const void* k_cache,
+                            const void* v_cache, const int32_t* pos0, int64_t S, int64_t Hq, int64_t Hkv,
+                            int64_t Lmax, float scale, float* part, int32_t* tickets, void* out) {
+  auto kern = D == 64 ? attention_kernel<T, 64> : attention_kernel<T, 128>;
+  return launch_pdl(kern, grid, dim3(kAttnWarps * 32), 0, st, (const T*)q, (const T*)k_cache, (const T*)v_cache,
+                    pos0, (int)S, (int)Hq, (int)Hkv, (int)Lmax, scale, part, tickets, (T*)out);
+}
+
 extern "C" int csaq_decode_attention(const void* q, const void* k_cache, const void* v_cache,
                                      const int32_t* pos0, int64_t B, int64_t S, int64_t Hq,
                                      int64_t Hkv, int64_t D, int64_t Lmax, float scale, float* part,
                                      int32_t* tickets, void* out, int dtype, void* stream) {
   if (!q || !k_cache || !v_cache || !pos0 || !part || !tickets || !out) return CSAQ_ERR_ARG;
-  if (D != 128) return CSAQ_ERR_UNSUPPORTED;
+  if (D != 128 && D != 64) return CSAQ_ERR_UNSUPPORTED;
   if (B <= 0 || S <= 0 || Hq <= 0 || Hkv <= 0 || Hq % Hkv || Lmax <= 0) return CSAQ_ERR_ARG;
   if (dtype != CSAQ_DT_F16 && dtype != CSAQ_DT_BF16) return CSAQ_ERR_ARG;
   const dim3 grid((unsigned)(B * Hkv), (unsigned)((Lmax + kChunk - 1) / kChunk));
   cudaStream_t st = as_stream(stream);
   if (dtype == CSAQ_DT_BF16)
-    return launch_pdl(attention_kernel<__nv_bfloat16>, dim3(grid), dim3(kAttnWarps * 32), 0, st, (const __nv_bfloat16*)q, (const __nv_bfloat16*)k_cache, (const __nv_bfloat16*)v_cache, pos0, (int)S, (int)Hq, (int)Hkv, (int)Lmax, scale, part, tickets, (__nv_bfloat16*)out);
-  else
-    return launch_pdl(attention_kernel<__half>, dim3(grid), dim3(kAttnWarps * 32), 0, st, (const __half*)q, (const __half*)k_cache, (const __half*)v_cache, pos0, (int)S, (int)Hq, (int)Hkv, (int)Lmax, scale, part, tickets, (__half*)out);
+    return launch_attention<__nv_bfloat16>(D, grid, st, q, k_cache, v_cache, pos0, S, Hq, Hkv, Lmax, scale, part,
+                                           tickets, out);
+  return launch_attention<__half>(D, grid, st, q, k_cache, v_cache, pos0, S, Hq, Hkv, Lmax, scale, part, tickets,
+                                  out);
 }
 
 extern "C" int csaq_silu_mul(const void* g, int64_t ldg, const void* u, int64_t ldu, void* h,

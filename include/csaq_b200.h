@@ -231,7 +231,7 @@ int csaq_rope_kv(const void* q, int64_t ldq, const void* k, int64_t ldk, const v
  * (keys 0..pos0[b]+s for token s), split over 64-key chunks; the last CTA of
  * a KV head merges the chunks. part: csaq_attention_workspace_floats floats;
  * tickets: B*Hkv int32, zero before the first call (calls leave them zero).
- * D must be 128. */
+ * D must be 64 or 128 (Qwen1.5-0.5B-shaped and Llama-shaped heads). */
 int64_t csaq_attention_workspace_floats(int64_t B, int64_t S, int64_t Hq, int64_t Hkv, int64_t D,
                                         int64_t Lmax);
 int csaq_decode_attention(const void* q, const void* k_cache, const void* v_cache,

@@ -38,12 +38,18 @@ def tiny_qwen2():
     return _quantized("tiny-qwen2", seed=5)
 
 
+@pytest.fixture(scope="module")
+def tiny_qwen2_d64():
+    """64-wide heads (hidden 256, 4 heads), the head width of Qwen1.5-0.5B."""
+    return _quantized("tiny-qwen2-d64", seed=6)
+
+
 def _prompt(B, P, V, seed=0):
     g = torch.Generator().manual_seed(seed)
     return torch.randint(0, V, (B, P), generator=g)
 
 
-@pytest.mark.parametrize("which", ["tiny_llama", "tiny_qwen2"])
+@pytest.mark.parametrize("which", ["tiny_llama", "tiny_qwen2", "tiny_qwen2_d64"])
 @pytest.mark.parametrize("verify", [False, True])
 def test_runtime_logits_match_hf(which, verify, request):
     from csaq.inference import CSAQInferenceEngine
@@ -86,10 +92,11 @@ def test_verify_weights_differ_from_draft(tiny_llama):
     assert (a - b).abs().max() > 0
 
 
-@pytest.mark.parametrize("B,K", [(1, 4), (3, 4), (2, 2)])
-def test_speculative_equals_greedy_verify(tiny_llama, B, K):
+@pytest.mark.parametrize("which,B,K", [("tiny_llama", 1, 4), ("tiny_llama", 3, 4), ("tiny_llama", 2, 2),
+                                       ("tiny_qwen2_d64", 2, 4)])
+def test_speculative_equals_greedy_verify(which, B, K, request):
     from csaq.inference import CSAQInferenceEngine
-    model, cmap, _ = tiny_llama
+    model, cmap, _ = request.getfixturevalue(which)
     V = model.config.vocab_size
     prompt = _prompt(B, 33, V, seed=7 + B)
     eng = CSAQInferenceEngine(model, cmap, verbose=False)
