@@ -199,8 +199,11 @@ int csaq_coact_counts(const uint32_t* bits, int64_t C, int64_t n_words, int64_t 
 int csaq_jaccard_bits(const int32_t* inter, int64_t ld_i, const int32_t* f, int64_t C,
                       float threshold, uint32_t* adj, int64_t ld_adj, void* stream);
 
-/* Seed-order greedy clique partition (csaq/core.py:268-285) on one CTA:
- * labels[c] = clique index of channel c in seed order; *n_cliques = count. */
+/* Seed-order greedy clique partition (csaq/core.py:268-285):
+ * labels[c] = clique index of channel c in seed order; *n_cliques = count.
+ * Bits of columns >= C are ignored. labels also serves as the call's scratch
+ * (per-row flags between its two launches), so it must not alias adj.
+ * C up to 1.6M channels (the taken set, C/8 bytes, lives in shared memory). */
 int csaq_greedy_cliques(const uint32_t* adj, int64_t ld_adj, int64_t C, int32_t* labels,
                         int32_t* n_cliques, void* stream);
 
