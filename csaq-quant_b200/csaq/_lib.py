@@ -14,7 +14,9 @@ from typing import Iterable, List, Optional, Sequence
 
 import torch
 
-LIB_PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), "lib", "libcsaq_b200.so")
+# CSAQ_LIB=checked loads the checked build (index guards, csaq_guard_report)
+LIB_PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), "lib",
+                        "libcsaq_b200_checked.so" if os.environ.get("CSAQ_LIB") == "checked" else "libcsaq_b200.so")
 
 CSAQ_OK = 0
 DT_F32, DT_F16, DT_BF16 = 0, 1, 2
@@ -72,6 +74,9 @@ _SIGNATURES = {
     "csaq_version": (ctypes.c_char_p, []),
     "csaq_status_string": (ctypes.c_char_p, [c_int]),
     "csaq_last_cuda_error": (c_int, []),
+    "csaq_checked_build": (c_int, []),
+    "csaq_guard_report": (c_int, [c_vp, c_vp, c_vp, c_vp]),
+    "csaq_guard_clear": (c_int, []),
     "csaq_packed_row_bytes": (c_i64, [c_i64, c_int]),
     "csaq_group_scales": (c_int, [c_vp, c_int, c_i64, c_i64, c_i64, c_int, c_i64, c_vp, c_vp, c_vp, c_vp]),
     "csaq_quant_pack_rows": (c_int, [c_vp, c_int, c_i64, c_i64, c_i64, c_int, c_i64, c_vp, c_vp, c_i64,

@@ -61,6 +61,49 @@ inline int launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t sm
   return launch_status();
 }
 
+// ── checked builds ──────────────────────────────────────────────────────────
+// Built with -DCSAQ_CHECKED, CSAQ_GUARD(ok, site, value, bound) counts a failed
+// index test in this translation unit's record, keeps the first failure's
+// site, value and bound, and yields false so that the caller skips the
+// access. A translation unit that uses it declares its record once with
+// CSAQ_GUARD_RECORD(), which also registers a host-side reader of the record
+// with the library (csaq_guard_report sums them). In the default build the
+// guard is the constant true and the record is empty: no code is added.
+#ifdef CSAQ_CHECKED
+void register_guard_reader(int (*read)(unsigned long long* count, long long* first), int (*clear)());
+#define CSAQ_GUARD_RECORD()                                                                             \
+  static __device__ unsigned long long g_guard_count;                                                   \
+  static __device__ long long g_guard_first[3];                                                         \
+  static __device__ __forceinline__ bool guard_check(bool ok, int site, long long v, long long bound) {  \
+    if (ok) return true;                                                                                \
+    if (atomicAdd(&g_guard_count, 1ull) == 0ull) {                                                      \
+      g_guard_first[0] = site;                                                                          \
+      g_guard_first[1] = v;                                                                             \
+      g_guard_first[2] = bound;                                                                         \
+    }                                                                                                   \
+    return false;                                                                                       \
+  }                                                                                                     \
+  static int guard_read(unsigned long long* count, long long* first) {                                  \
+    if (cudaMemcpyFromSymbol(count, g_guard_count, sizeof(*count)) != cudaSuccess ||                    \
+        cudaMemcpyFromSymbol(first, g_guard_first, 3 * sizeof(long long)) != cudaSuccess)               \
+      return launch_status();                                                                           \
+    return CSAQ_OK;                                                                                     \
+  }                                                                                                     \
+  static int guard_clear() {                                                                            \
+    const unsigned long long z = 0ull;                                                                  \
+    const long long zf[3] = {0, 0, 0};                                                                  \
+    if (cudaMemcpyToSymbol(g_guard_count, &z, sizeof(z)) != cudaSuccess ||                              \
+        cudaMemcpyToSymbol(g_guard_first, zf, sizeof(zf)) != cudaSuccess)                               \
+      return launch_status();                                                                           \
+    return CSAQ_OK;                                                                                     \
+  }                                                                                                     \
+  static const bool g_guard_registered = (register_guard_reader(guard_read, guard_clear), true);
+#define CSAQ_GUARD(ok, site, v, bound) guard_check((ok), (site), (long long)(v), (long long)(bound))
+#else
+#define CSAQ_GUARD_RECORD()
+#define CSAQ_GUARD(ok, site, v, bound) true
+#endif
+
 inline int dtype_size(int dt) {
   switch (dt) {
     case CSAQ_DT_F32: return 4;

@@ -43,6 +43,8 @@
 namespace csaq {
 namespace {
 
+CSAQ_GUARD_RECORD()
+
 constexpr int kBM = 256;                   // tokens per tile (two MMAs of M = 128)
 constexpr int kBN = 256;                   // weight rows per tile (MMA N)
 constexpr int kBK = 64;                    // columns per step (one 128-byte swizzle row of bf16)
@@ -453,8 +455,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int j = 0; j < 32; ++j) buf[lane * 33 + j] = __uint_as_float(v[j]);  // [token][row]
         __syncwarp();
         const int row = row0 + cb + lane;  // lane = tier row
-        const bool rlive = row < T.n_rows;
-        const int orow = rlive ? T.out_rows[row] : 0;
+        const int orow = row < T.n_rows ? T.out_rows[row] : 0;
+        const bool rlive = row < T.n_rows &&
+                           CSAQ_GUARD(orow >= 0 && orow < T.ldy && (!T.residual || orow < T.ldr),
+                                      CSAQ_GUARD_GEMM_OUT_ROW, orow, T.ldy);
         const float bv = (rlive && T.bias) ? to_f32<ACT>(reinterpret_cast<const ACT*>(T.bias)[orow]) : 0.0f;
         const int nt_w = M - tokw < 32 ? (int)(M - tokw) : 32;
         for (int t = 0; t < nt_w; ++t) {

@@ -350,10 +350,15 @@ struct OutDesc {
   int n_rows;
 };
 
+CSAQ_GUARD_RECORD()
+
 template <typename ACT, typename TD>
 __device__ __forceinline__ void store_out(const TD& T, int row, int tok, float v, float xe) {
   v = __fmul_rn(v, xe);
   const int orow = T.out_rows[row];
+  if (!CSAQ_GUARD(orow >= 0 && orow < T.ldy && (!T.residual || orow < T.ldr), CSAQ_GUARD_GEMV_OUT_ROW, orow,
+                  T.ldy))
+    return;
   if (T.bias) v = __fadd_rn(v, to_f32<ACT>(reinterpret_cast<const ACT*>(T.bias)[orow]));
   if (T.residual)
     v = __fadd_rn(v, to_f32<ACT>(reinterpret_cast<const ACT*>(T.residual)[(int64_t)tok * T.ldr + orow]));
@@ -954,8 +959,9 @@ __global__ void qgemv_simt_kernel(const __grid_constant__ TierParams P, int64_t 
     float v = 0.0f;
 #pragma unroll
     for (int j = 0; j < 8; ++j) if (j == lane) v = acc[j];
-    if (tok < M) {
-      const int orow = T.out_rows[row];
+    const int orow = tok < M ? T.out_rows[row] : 0;
+    if (tok < M && CSAQ_GUARD(orow >= 0 && orow < T.ldy && (!T.residual || orow < T.ldr), CSAQ_GUARD_GEMV_OUT_ROW,
+                              orow, T.ldy)) {
       if (T.bias) v += to_f32<ACT>(reinterpret_cast<const ACT*>(T.bias)[orow]);
       if (T.residual) v += to_f32<ACT>(reinterpret_cast<const ACT*>(T.residual)[(int64_t)tok * T.ldr + orow]);
       reinterpret_cast<ACT*>(T.y)[(int64_t)tok * T.ldy + orow] = from_f32<ACT>(v);

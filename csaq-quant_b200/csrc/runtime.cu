@@ -14,6 +14,8 @@
 namespace csaq {
 namespace {
 
+CSAQ_GUARD_RECORD()
+
 template <typename T>
 __device__ __forceinline__ float round_to(float v) {
   return to_f32<T>(from_f32<T>(v));
@@ -129,6 +131,7 @@ __global__ void rope_kv_kernel(const T* __restrict__ q, int64_t ldq, const T* __
   const int64_t m = blockIdx.y;  // token
   const int b = (int)(m / S), s = (int)(m % S);
   const int pos = pos0[b] + s;
+  if (!CSAQ_GUARD(pos >= 0 && pos < Lmax, CSAQ_GUARD_ROPE_POS, pos, Lmax)) return;
   const int half = D / 2, gpr = half / 8;  // 8-pair groups per head
   const int rot = (Hq + Hkv) * gpr;          // rotation work items of the token
   const int cpy = Hkv * (D / 8);             // value vectors of the token
@@ -208,6 +211,9 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attention_kernel(
   // values are copied before waiting, the new ones (written by the
   // predecessor) after
   const int p0 = pos0[b];
+  // every CTA of this head sees the same p0, so all of them skip together and
+  // the merge ticket stays consistent
+  if (!CSAQ_GUARD(p0 >= 0 && p0 + S <= Lmax, CSAQ_GUARD_ATTN_POS, p0, Lmax - S)) return;
   const int len = p0 + S;  // keys visible to the last new token
   const int k0 = sp * kChunk;
   __shared__ __align__(16) T ks[kChunk][D];

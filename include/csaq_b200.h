@@ -40,6 +40,21 @@ const char* csaq_version(void);
 const char* csaq_status_string(int status);
 int csaq_last_cuda_error(void);   /* cudaError_t of the last failed launch in this thread */
 
+/* Checked builds. libcsaq_b200_checked.so (build.py --checked) tests the
+ * indices that kernels take from caller data before using them; a failed
+ * test is counted, the first one is recorded (site, value, bound) and the
+ * access is skipped. The default library has no such tests and reports
+ * CSAQ_ERR_UNSUPPORTED from csaq_guard_report / csaq_guard_clear. */
+enum {
+  CSAQ_GUARD_GEMV_OUT_ROW = 1,  /* csaq_qgemv: out_rows[i] outside [0, ldy) (or [0, ldr) with a residual) */
+  CSAQ_GUARD_GEMM_OUT_ROW = 2,  /* csaq_qgemm: the same                                               */
+  CSAQ_GUARD_ROPE_POS = 3,      /* csaq_rope_kv: position pos0[b] + s outside [0, Lmax)                */
+  CSAQ_GUARD_ATTN_POS = 4       /* csaq_decode_attention: pos0[b] < 0 or pos0[b] + S > Lmax           */
+};
+int csaq_checked_build(void);     /* 1 for the checked library, else 0 */
+int csaq_guard_report(int64_t* count, int64_t* site, int64_t* value, int64_t* bound);
+int csaq_guard_clear(void);
+
 /* ── Quantisation primitives ─────────────────────────────────────────────── */
 
 /* Packed bytes per row: replaces the cols_packed arithmetic of

@@ -58,6 +58,27 @@ def test_version_and_status_strings():
     assert L.csaq_packed_row_bytes(37, 3) == -1
 
 
+def test_checked_build_switch():
+    """The default library has no index guards; libcsaq_b200_checked.so
+    (CSAQ_LIB=checked) reports itself as checked and exports the same ABI."""
+    import subprocess
+    import sys
+    from csaq import _lib
+    L = _lib.lib()
+    assert L.csaq_checked_build() == 0
+    v = [ctypes.c_int64(7) for _ in range(4)]
+    assert L.csaq_guard_report(*[ctypes.byref(x) for x in v]) == -5
+    assert [x.value for x in v] == [0, 0, 0, 0]
+    assert L.csaq_guard_clear() == -5
+    assert L.csaq_guard_report(None, None, None, None) == -1
+    code = ("import sys; sys.path.insert(0, 'csaq-quant_b200'); from csaq import _lib; "
+            "L = _lib.lib(); print(L.csaq_checked_build(), _lib.LIB_PATH.endswith('_checked.so'))")
+    r = subprocess.run([sys.executable, "-c", code], capture_output=True, text=True, timeout=300,
+                       env=dict(os.environ, CSAQ_LIB="checked"), cwd=REPO)
+    assert r.returncode == 0, r.stderr[-2000:]
+    assert r.stdout.split() == ["1", "True"]
+
+
 def test_argument_validation_without_launch():
     """Bad arguments are rejected on the host before any kernel launch."""
     from csaq import _lib
