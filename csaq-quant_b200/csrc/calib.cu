@@ -176,13 +176,37 @@ __global__ void __launch_bounds__(256) coact_kernel(const uint32_t* __restrict__
       sb[ww][ch] = (cj < C && w < n_words) ? bits[cj * ld_bits + w] : 0u;
     }
     __syncthreads();
-#pragma unroll 8
-    for (int ww = 0; ww < kWordsPerStage; ++ww) {
+    // Three words at a time through a carry-save step: for x, y, z
+    // popc(x) + popc(y) + popc(z) = popc(x ^ y ^ z) + 2 popc(maj(x, y, z)),
+    // exact in integers. Two population counts (the XU pipe, 16 per SM and
+    // clock, the kernel's bound) replace three; the XOR and majority are one
+    // LOP3 each on the ALU pipe, which has room.
+#pragma unroll 1
+    for (int ww = 0; ww + 3 <= kWordsPerStage; ww += 3) {
+      uint32_t a[3][4], b[3][4];
+#pragma unroll
+      for (int t = 0; t < 3; ++t)
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          a[t][q] = sa[ww + t][ty + 16 * q];  // broadcast within a half-warp
+          b[t][q] = sb[ww + t][tx + 16 * q];  // 16 consecutive banks
+        }
+#pragma unroll
+      for (int p = 0; p < 4; ++p)
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const uint32_t x = a[0][p] & b[0][q], y = a[1][p] & b[1][q], z = a[2][p] & b[2][q];
+          const uint32_t sum = x ^ y ^ z, carry = (x & y) | (z & (x ^ y));
+          acc[p][q] += __popc(sum) + 2u * __popc(carry);
+        }
+    }
+#pragma unroll
+    for (int ww = kWordsPerStage / 3 * 3; ww < kWordsPerStage; ++ww) {
       uint32_t a[4], b[4];
 #pragma unroll
       for (int q = 0; q < 4; ++q) {
-        a[q] = sa[ww][ty + 16 * q];  // broadcast within a half-warp
-        b[q] = sb[ww][tx + 16 * q];  // 16 consecutive banks
+        a[q] = sa[ww][ty + 16 * q];
+        b[q] = sb[ww][tx + 16 * q];
       }
 #pragma unroll
       for (int p = 0; p < 4; ++p)
