@@ -1,7 +1,8 @@
 """The reference-facing Python API on the CPU: module paths and names,
 CSAQConfig validation (csaq/config.py:19-145), the unsupported-bits
 ValueError raised before any device work (csaq/kernels.py:488-492, 569, 600),
-and the SpeculativeReport arithmetic (csaq/inference.py:37-111)."""
+the SpeculativeReport arithmetic (csaq/inference.py:37-111), and the
+calibration-data, perplexity and report helpers (csaq/utils.py:25-218)."""
 
 import math
 import warnings
@@ -105,3 +106,68 @@ def test_speculative_report_arithmetic():
     assert s["mode"] == "speculative" and s["p95_latency_ms"] == "nan" and s["tokens_per_second"] == 80.0
     empty = SpeculativeReport()
     assert empty.acceptance_rate == 0.0 and empty.tokens_per_second == 0.0
+
+
+class _Encoding(dict):
+    """A dict whose keys also read as attributes, like HF's BatchEncoding."""
+
+    def __getattr__(self, k):
+        return self[k]
+
+
+class _FakeTokenizer:
+    """Characters -> ids, with the HF call signature the helpers use."""
+
+    def __call__(self, text, return_tensors="pt", max_length=None, truncation=False, padding=None):
+        ids = [ord(c) % 97 + 1 for c in text]
+        if truncation and max_length is not None:
+            ids = ids[:max_length]
+        mask = [1] * len(ids)
+        if padding == "max_length" and max_length is not None:
+            mask += [0] * (max_length - len(ids))
+            ids += [0] * (max_length - len(ids))
+
+        return _Encoding(input_ids=torch.tensor([ids]), attention_mask=torch.tensor([mask]))
+
+
+def test_calibration_data_and_report(tmp_path):
+    import json
+    from csaq.utils import build_calibration_data, generate_csaq_report
+    with pytest.raises(ValueError, match="custom_texts is empty"):
+        build_calibration_data(_FakeTokenizer(), [])
+    with pytest.warns(UserWarning, match="Only 3 calibration samples"):
+        batches = build_calibration_data(_FakeTokenizer(), ["abc", "a much longer sentence here", "x"], seq_len=8)
+    assert len(batches) == 3 and all(b["input_ids"].shape == (1, 8) for b in batches)
+    assert int(batches[0]["attention_mask"].sum()) == 3 and int(batches[1]["attention_mask"].sum()) == 8
+    assert len(build_calibration_data(_FakeTokenizer(), ["t"] * 20, n=16)) == 16
+    info = {"tier_stats": {"int4": 300, "int8": 100}, "actual_bits": 5.0, "cliques_count": 12, "elapsed_s": 1.234}
+    rep = generate_csaq_report(info, str(tmp_path / "r" / "CSAQ_Report.json"))
+    assert rep["bit_distribution_pct"] == {"int4": 75.0, "int8": 25.0}
+    assert rep["total_quantized_params"] == 400 and rep["ppl"] == "not_computed"
+    assert json.load(open(tmp_path / "r" / "CSAQ_Report.json")) == rep
+
+
+def test_perplexity_on_a_cpu_model():
+    from csaq.utils import compute_perplexity
+
+    class _Uniform(torch.nn.Module):
+        """Uniform logits over 100 tokens: the loss is ln(100) for any input."""
+
+        def __init__(self):
+            super().__init__()
+            self.w = torch.nn.Parameter(torch.zeros(1))
+
+        def forward(self, ids, labels=None):
+            logits = torch.zeros(ids.shape[0], ids.shape[1], 100) + self.w
+            loss = torch.nn.functional.cross_entropy(logits[:, :-1].reshape(-1, 100), labels[:, 1:].reshape(-1))
+
+            class _Out:
+                pass
+            o = _Out()
+            o.loss = loss
+            return o
+
+    ppl = compute_perplexity(_Uniform(), _FakeTokenizer(), ["some evaluation text"] * 3, seq_len=16, stride=8)
+    assert ppl == pytest.approx(100.0, rel=1e-5)
+    with pytest.raises(ValueError):
+        compute_perplexity(_Uniform(), _FakeTokenizer(), [])
