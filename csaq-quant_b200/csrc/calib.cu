@@ -288,7 +288,8 @@ __global__ void jaccard_bits_kernel(const int32_t* __restrict__ inter, int64_t l
 // Pass 1 (row_tail_kernel, parallel): flag[i] = row i has a bit above the
 // diagonal, i.e. seed i may take members. The flags are written into labels,
 // which pass 2 overwrites.
-// Pass 2 (greedy_seq_kernel, one warp): walks the seeds 32 at a time (one word
+// Pass 2, for C above what greedy_runs_kernel below serves (greedy_seq_kernel,
+// one warp): walks the seeds 32 at a time (one word
 // of channels). The taken bits of the current word live in a register; a
 // seed without a flag costs a few register operations, and only flagged
 // seeds read their row (L2-resident after pass 1) and update the taken set of
@@ -365,6 +366,84 @@ __global__ void __launch_bounds__(32) greedy_seq_kernel(const uint32_t* __restri
       ++id;
     }
     if (lane < nb && !((taken0 >> lane) & 1u)) labels[i0 + lane] = my;
+    __syncwarp();
+  }
+  if (lane == 0) *n_cliques = id;
+}
+
+// Pass 2 when both bit sets fit shared memory (C <= kRunMaxChannels): the
+// same walk, but a run of open seeds without a flag (they take no members,
+// so each is a singleton clique) is labelled in one step: lane l of the run
+// gets id + the number of run seeds below it. Only flagged seeds cost a row
+// read. The whole CTA first packs the flags (labels on entry) into a bit set,
+// so the walk never waits on a global load for them.
+constexpr int kRunMaxChannels = 819200;  // 2 bit sets of C/8 bytes in 200 KB
+
+__global__ void __launch_bounds__(1024) greedy_runs_kernel(const uint32_t* __restrict__ adj, int64_t ld_adj,
+                                                           int C, int32_t* labels,
+                                                           int32_t* __restrict__ n_cliques) {
+  extern __shared__ uint32_t bitsets[];
+  const int words = (C + 31) / 32;
+  uint32_t* taken_s = bitsets;
+  uint32_t* flag_s = bitsets + words;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, n_warps = blockDim.x >> 5;
+  for (int w = warp; w < words; w += n_warps) {
+    const int c = w * 32 + lane;
+    const uint32_t f = __ballot_sync(0xffffffffu, c < C && labels[c] != 0);
+    if (lane == 0) {
+      flag_s[w] = f;
+      taken_s[w] = 0u;
+    }
+  }
+  __syncthreads();
+  if (warp != 0) return;
+  const uint32_t last = (C & 31) ? (1u << (C & 31)) - 1u : 0xffffffffu;
+  const uint32_t below = (1u << lane) - 1u;
+  int id = 0;
+  for (int w0 = 0; w0 < words; ++w0) {
+    const int i0 = w0 * 32;
+    const uint32_t valid = w0 == words - 1 ? last : 0xffffffffu;
+    const uint32_t flagged = flag_s[w0];
+    uint32_t tw = taken_s[w0];  // uniform across the warp from here on
+    const uint32_t taken0 = tw;
+    int my = 0;
+    while (true) {
+      const uint32_t open = ~tw & valid;
+      if (!open) break;
+      const uint32_t fl = open & flagged;
+      const uint32_t run = fl ? (open & ((fl & (0u - fl)) - 1u)) : open;  // singletons before the next flagged seed
+      if ((run >> lane) & 1u) my = id + __popc(run & below);
+      id += __popc(run);
+      tw |= run;
+      if (!fl) break;
+      const int b = __ffs(fl) - 1;
+      tw |= 1u << b;
+      if (lane == b) my = id;
+      const uint32_t* row = adj + (int64_t)(i0 + b) * ld_adj;
+      const uint32_t r0 = row[w0];
+      int w = w0 + 1 + lane;
+      uint32_t r = w < words ? row[w] : 0u;
+      const uint32_t m0 = r0 & ~tw & ~((2u << b) - 1u) & valid;
+      tw |= m0;
+      if ((m0 >> lane) & 1u) my = id;
+      for (; w < words; w += 32) {
+        const uint32_t rn = w + 32 < words ? row[w + 32] : 0u;
+        uint32_t m = r & ~taken_s[w];
+        if (w == words - 1) m &= last;
+        if (m) {
+          taken_s[w] |= m;
+          do {
+            const int bb = __ffs(m) - 1;
+            m &= m - 1;
+            labels[w * 32 + bb] = id;
+          } while (m);
+        }
+        r = rn;
+      }
+      __syncwarp();
+      ++id;
+    }
+    if (((valid & ~taken0) >> lane) & 1u) labels[i0 + lane] = my;
     __syncwarp();
   }
   if (lane == 0) *n_cliques = id;
@@ -507,12 +586,20 @@ extern "C" int csaq_greedy_cliques(const uint32_t* adj, int64_t ld_adj, int64_t 
   row_tail_kernel<<<blocks_for(C * 32), kThreads, 0, st>>>(adj, ld_adj, C, labels);
   int rc = launch_status();
   if (rc) return rc;
-  const size_t smem = (size_t)words * 4;
-  if (smem > 48 * 1024) {
-    if (cudaFuncSetAttribute(greedy_seq_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
-        cudaSuccess)
-      return launch_status();
+  if (C <= kRunMaxChannels) {
+    const size_t smem = (size_t)words * 8;
+    if (smem > 48 * 1024) {
+      if (cudaFuncSetAttribute(greedy_runs_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
+          cudaSuccess)
+        return launch_status();
+    }
+    greedy_runs_kernel<<<1, 1024, smem, st>>>(adj, ld_adj, (int)C, labels, n_cliques);
+    return launch_status();
   }
+  const size_t smem = (size_t)words * 4;
+  if (cudaFuncSetAttribute(greedy_seq_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
+      cudaSuccess)
+    return launch_status();
   greedy_seq_kernel<<<1, 32, smem, st>>>(adj, ld_adj, (int)C, labels, n_cliques);
   return launch_status();
 }

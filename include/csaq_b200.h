@@ -218,7 +218,8 @@ int csaq_jaccard_bits(const int32_t* inter, int64_t ld_i, const int32_t* f, int6
  * labels[c] = clique index of channel c in seed order; *n_cliques = count.
  * Bits of columns >= C are ignored. labels also serves as the call's scratch
  * (per-row flags between its two launches), so it must not alias adj.
- * C up to 1.6M channels (the taken set, C/8 bytes, lives in shared memory). */
+ * C up to 1.6M channels (the taken set, C/8 bytes, lives in shared memory;
+ * up to 819,200 channels singleton runs are labelled a word at a time). */
 int csaq_greedy_cliques(const uint32_t* adj, int64_t ld_adj, int64_t C, int32_t* labels,
                         int32_t* n_cliques, void* stream);
 
