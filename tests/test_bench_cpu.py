@@ -42,3 +42,13 @@ def test_reference_arm_other_ranks_exit_without_output():
                        env=_env(RANK="1", WORLD_SIZE="2", LOCAL_RANK="1"), cwd=REPO)
     assert r.returncode == 0, r.stderr[-2000:]
     assert r.stdout.strip() == ""
+
+
+def test_cpu_baseline_samples_of_the_kernel_workloads():
+    """The host-core legs of the gemm and calib workloads run one pass at budget 0."""
+    sys.path.insert(0, REPO)
+    import bench
+    tf, desc = bench.cpu_gemm_sample(0.0)
+    assert tf > 0 and desc.startswith("1 dequantise-then-matmul passes")
+    gbs, desc = bench.cpu_salience_sample(0.0)
+    assert gbs > 0 and desc.startswith("1 accumulation passes")
