@@ -22,11 +22,15 @@ rows carry the bit-width the solver gave their clique.
 
 from __future__ import annotations
 
+import contextlib
+import gc
+import math
 import time
 import warnings
 from collections import defaultdict
 from typing import Any, Dict, Iterator, List, Optional, Tuple, Union
 
+import numpy as np
 import torch
 import torch.nn as nn
 
@@ -333,6 +337,23 @@ class CausalProfiler:
 # Phase 3: solver (csaq/core.py:294-361)
 # ─────────────────────────────────────────────────────────────────────────────
 
+_SCAN_WINDOW = 65536  # cliques per cumulative-sum window of the upgrade scan
+
+
+@contextlib.contextmanager
+def _gc_paused() -> Iterator[None]:
+    """Pause Python's cyclic garbage collector while a large acyclic result
+    (millions of small dicts and lists) is built; its collections would
+    otherwise rescan the growing result several times over."""
+    was = gc.isenabled()
+    gc.disable()
+    try:
+        yield
+    finally:
+        if was:
+            gc.enable()
+
+
 def solve_clique_budget(salience: SalienceMap, cliques: CliqueMap,
                         config: CSAQConfig) -> Tuple[BudgetMap, Dict[str, int], float]:
     """Assign bit-widths to cliques to hit config.target_bits on average.
@@ -343,10 +364,30 @@ def solve_clique_budget(salience: SalienceMap, cliques: CliqueMap,
     option, then each clique in order takes upgrades while the running total
     stays within target_bits * elements. Per-clique sums are taken on the
     device in one pass per layer.
+
+    The upgrade pass is a scan, not a loop over cliques. In order, clique i
+    reaches the largest option o with (o - b_i) * e_i <= R_i, where R_i is
+    the budget left (the reference's step-by-step upgrades accept exactly
+    that prefix of options). A run of cliques that all reach their top
+    option while the budget lasts is one cumulative sum; only the clique that
+    ends a run is resolved on its own, and each such clique takes part of
+    what is left. All budget arithmetic is in integers: an integer total fits
+    under target_bits * elements iff it fits under its floor.
     """
+    with _gc_paused():
+        return _solve_clique_budget(salience, cliques, config)
+
+
+def _solve_clique_budget(salience: SalienceMap, cliques: CliqueMap,
+                         config: CSAQConfig) -> Tuple[BudgetMap, Dict[str, int], float]:
     options = sorted(config.bit_options)
-    min_bits = options[0]
-    recs = []  # (layer, rows, salience, elems, leader)
+    min_bits, max_bits = options[0], options[-1]
+    layer_names: List[str] = []
+    layer_counts: List[int] = []
+    rows_all: List[List[int]] = []
+    sal_all: List[float] = []
+    elems_all: List[int] = []
+    lead_all: List[int] = []
     for name, layer_cliques in cliques.items():
         s = salience[name]
         if not layer_cliques:
@@ -355,14 +396,10 @@ def solve_clique_budget(salience: SalienceMap, cliques: CliqueMap,
             s = s.float()
         C, K = s.shape
         row_sal = s.sum(dim=1)
-        lab = torch.empty(C, dtype=torch.int64)
-        flat, starts = [], []
-        for ci, c in enumerate(layer_cliques):
-            starts.append(len(flat))
-            flat.extend(c)
-        idx = torch.tensor(flat, dtype=torch.int64, device=s.device)
+        sizes = [len(c) for c in layer_cliques]
+        idx = torch.tensor([r for c in layer_cliques for r in c], dtype=torch.int64, device=s.device)
         seg = torch.repeat_interleave(torch.arange(len(layer_cliques), device=s.device),
-                                      torch.tensor([len(c) for c in layer_cliques], device=s.device))
+                                      torch.tensor(sizes, device=s.device))
         rs = row_sal[idx]
         c_sal = torch.zeros(len(layer_cliques), dtype=torch.float32, device=s.device).index_add_(0, seg, rs)
         # leader: first row of maximal row salience inside the clique
@@ -373,42 +410,79 @@ def solve_clique_budget(salience: SalienceMap, cliques: CliqueMap,
         first = torch.full((len(layer_cliques),), idx.numel(), dtype=torch.int64, device=s.device)
         first = first.scatter_reduce(0, seg, torch.where(is_max, pos_in, torch.full_like(pos_in, idx.numel())),
                                      reduce="amin")
-        leaders = idx[first.clamp(max=idx.numel() - 1)].cpu().tolist()
-        c_sal = c_sal.cpu().tolist()
-        for ci, c in enumerate(layer_cliques):
-            recs.append((name, c, float(c_sal[ci]), len(c) * K, int(leaders[ci])))
-    if not recs:
+        lead_all.extend(idx[first.clamp(max=idx.numel() - 1)].cpu().tolist())
+        sal_all.extend(c_sal.cpu().tolist())
+        layer_names.append(name)
+        layer_counts.append(len(layer_cliques))
+        rows_all.extend(layer_cliques)
+        elems_all.extend(n * K for n in sizes)
+    n = len(rows_all)
+    if n == 0:
         return {}, {}, float(config.target_bits)
-    total = sum(r[3] for r in recs)
-    bits = [min_bits] * len(recs)
-    current = sum(r[3] * min_bits for r in recs)
+    elems = np.asarray(elems_all, dtype=np.int64)
+    dens = np.asarray(sal_all, dtype=np.float64) / np.maximum(elems, 1)
+    total = int(elems.sum())
     target_total = config.target_bits * total
-    order = sorted(range(len(recs)), key=lambda i: recs[i][2] / max(recs[i][3], 1), reverse=True)
-    n_protect = max(1, int(config.protection_floor * len(recs)))
-    floor_target = min(8, max(options))
-    for i in order[:n_protect]:
-        fb = max(bits[i], floor_target)
-        if fb > bits[i] and fb in options:
-            current += (fb - bits[i]) * recs[i][3]
-            bits[i] = fb
-    for i in order:
-        for b in options:
-            if b <= bits[i]:
-                continue
-            cost = (b - bits[i]) * recs[i][3]
-            if current + cost <= target_total:
-                current += cost
-                bits[i] = b
-            else:
+    if np.isnan(dens).any():  # NaN keys: keep the reference's comparison sort
+        order = np.asarray(sorted(range(n), key=lambda i: dens[i], reverse=True), dtype=np.int64)
+    else:
+        order = np.argsort(-dens, kind="stable")
+    e = elems[order]
+    b = np.full(n, min_bits, dtype=np.int64)  # bits in `order`
+    current = min_bits * total
+    n_protect = max(1, int(config.protection_floor * n))
+    floor_target = min(8, max_bits)
+    if floor_target in options and floor_target > min_bits:
+        k = min(n_protect, n)
+        current += (floor_target - min_bits) * int(e[:k].sum())
+        b[:k] = floor_target
+    # upgrades: increments to the top option and to the next option
+    opts = np.asarray(options, dtype=np.int64)
+    nxt = opts[np.minimum(np.searchsorted(opts, b, side="right"), len(opts) - 1)]
+    inc_max = (max_bits - b) * e
+    inc_min = np.where(b < max_bits, (nxt - b) * e, np.iinfo(np.int64).max)
+    suffix_min = np.minimum.accumulate(inc_min[::-1])[::-1]
+    final = b.copy()
+    R = (math.floor(target_total) if math.isfinite(target_total) else 0) - current
+    i, window = 0, _SCAN_WINDOW
+    while i < n and R >= suffix_min[i]:
+        j_end = min(n, i + window)
+        cand = inc_min[i:j_end] <= R
+        cons = np.where(cand, inc_max[i:j_end], 0)
+        cs = np.cumsum(cons)
+        over = np.flatnonzero(cs > R)
+        q = int(over[0]) if over.size else j_end - i
+        final[i:i + q][cand[:q]] = max_bits
+        if q:
+            R -= int(cs[q - 1])
+        if not over.size:
+            i = j_end
+            continue
+        j = i + q  # its top option no longer fits: the largest that does
+        for o in options[::-1]:
+            if o > b[j] and (o - int(b[j])) * int(e[j]) <= R:
+                final[j] = o
+                R -= (o - int(b[j])) * int(e[j])
                 break
-    budget: BudgetMap = defaultdict(list)
-    stats: Dict[str, int] = defaultdict(int)
-    for i in order:
-        name, rows, sal, elems, leader = recs[i]
-        budget[name].append({"layer": name, "rows": rows, "salience": sal, "elems": elems,
-                             "bits": bits[i], "leader": leader})
-        stats[f"int{bits[i]}"] += elems
-    return dict(budget), dict(stats), current / max(total, 1)
+        i = j + 1
+    # dict keys in first-use order along `order`, as the reference's loop inserts them
+    used_bits = [(int(np.argmax(final == o)), o) for o in options if (final == o).any()]
+    stats = {f"int{o}": int(e[final == o].sum()) for _, o in sorted(used_bits)}
+    # per layer, its cliques in the global order (a stable sort keeps that order inside a layer,
+    # so a layer's first entry is where it first appears along `order`)
+    layer_of = np.repeat(np.arange(len(layer_names)), layer_counts)[order]
+    grouped = np.argsort(layer_of, kind="stable")
+    g_order, g_final = order[grouped].tolist(), final[grouped].tolist()
+    starts = np.concatenate([[0], np.cumsum(layer_counts)]).tolist()
+    first_pos = grouped[np.asarray(starts[:-1], dtype=np.int64)]
+    budget: BudgetMap = {}
+    for li in np.argsort(first_pos, kind="stable").tolist():
+        nm, a, z = layer_names[li], starts[li], starts[li + 1]
+        budget[nm] = [{"layer": nm, "rows": rows_all[oi], "salience": sal_all[oi], "elems": elems_all[oi],
+                       "bits": bt, "leader": lead_all[oi]}
+                      for oi, bt in zip(g_order[a:z], g_final[a:z])]
+    used = int((final * e).sum())
+    return budget, stats, used / max(total, 1)
 
 
 # ─────────────────────────────────────────────────────────────────────────────
