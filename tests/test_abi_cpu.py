@@ -79,6 +79,32 @@ def test_checked_build_switch():
     assert r.stdout.split() == ["1", "True"]
 
 
+def test_c_consumer_compiles_links_and_runs(tmp_path):
+    """include/csaq_b200.h compiles as strict C99 and a C program linked to the
+    library gets the same host-side answers as the Python binding."""
+    import shutil
+    import subprocess
+    gcc = shutil.which("gcc")
+    if gcc is None:
+        pytest.skip("no C compiler")
+    lib_dir = os.path.join(REPO, "csaq-quant_b200", "csaq", "lib")
+    exe = str(tmp_path / "abi_c_consumer")
+    r = subprocess.run([gcc, "-std=c99", "-Wall", "-Wextra", "-pedantic", "-Werror", "-I", os.path.join(REPO, "include"),
+                        os.path.join(REPO, "tests", "abi_c_consumer.c"), "-L", lib_dir, "-lcsaq_b200",
+                        f"-Wl,-rpath,{lib_dir}", "-o", exe], capture_output=True, text=True, timeout=120)
+    assert r.returncode == 0, r.stderr
+    out = subprocess.run([exe], capture_output=True, text=True, timeout=120)
+    assert out.returncode == 0, out.stderr
+    lines = dict(l.split(" ", 1) for l in out.stdout.strip().splitlines())
+    assert "sm_100a" in lines["version"]
+    assert lines["status"] == "unsupported bit-width"
+    assert lines["row_bytes"] == "10 19 37 74"
+    assert lines["quant_pack_null"] == "-1" and lines["quant_pack_bits"] == "-2"
+    assert lines["qgemv_bits"] == "-2" and lines["qgemv_tiers"] == "-1"
+    assert lines["greedy_null"] == "-1"
+    assert lines["checked"] == "0 guard -5"
+
+
 def test_argument_validation_without_launch():
     """Bad arguments are rejected on the host before any kernel launch."""
     from csaq import _lib
