@@ -35,12 +35,13 @@ enum {
 
 enum { CSAQ_DT_F32 = 0, CSAQ_DT_F16 = 1, CSAQ_DT_BF16 = 2 };
 
-/* Library identification and diagnostics. */
+/* Library identification and diagnostics (no reference counterpart). */
 const char* csaq_version(void);
 const char* csaq_status_string(int status);
 int csaq_last_cuda_error(void);   /* cudaError_t of the last failed launch in this thread */
 
-/* Checked builds. libcsaq_b200_checked.so (build.py --checked) tests the
+/* Checked builds (no reference counterpart: the reference has no device
+ * code). libcsaq_b200_checked.so (build.py --checked) tests the
  * indices that kernels take from caller data before using them; a failed
  * test is counted, the first one is recorded (site, value, bound) and the
  * access is skipped. The default library has no such tests and reports
@@ -175,7 +176,8 @@ int csaq_qgemv(const csaq_tier* tiers, int n_tiers, int64_t K, const void* x, in
  * bytes (8 for 2-bit tiers) (else CSAQ_ERR_UNSUPPORTED). One launch per tier. */
 int csaq_qgemm(const csaq_tier* tiers, int n_tiers, int64_t K, const void* x, int x_dtype, int64_t M,
                int64_t ldx, void* stream);
-/* CTAs of csaq_qgemm whose bounded wait for the tensor core gave up (diagnostic). */
+/* CTAs of csaq_qgemm whose bounded wait for the tensor core gave up
+ * (diagnostic; no reference counterpart). */
 int csaq_qgemm_wait_timeouts(int64_t* count);
 
 /* Number of warps, since the library was loaded on this device, whose bounded
@@ -184,8 +186,9 @@ int csaq_qgemm_wait_timeouts(int64_t* count);
  * counterpart in the reference (its kernels have no device-side waits). */
 int csaq_qgemv_wait_timeouts(int64_t* count);
 
-/* Same contract, always the CUDA-core kernel (any K, any group size, any M);
- * a second GPU path used to cross-check the tensor-core kernel. */
+/* Same contract as csaq_qgemv (the forward of csaq/kernels.py:450-475),
+ * always the CUDA-core kernel (any K, any group size, any M); a second GPU
+ * path used to cross-check the tensor-core kernel. */
 int csaq_qgemv_simt(const csaq_tier* tiers, int n_tiers, int64_t K, const void* x, int x_dtype,
                     int64_t M, int64_t ldx, void* stream);
 
@@ -358,7 +361,9 @@ int csaq_spec_sample_verify(const int64_t* draft, const void* draft_logits, cons
                             float temperature, float top_p, uint64_t seed, uint64_t* counter, int64_t* vt,
                             int dtype, void* stream);
 
-/* Bookkeeping of one plain greedy decode step. */
+/* Bookkeeping of one plain greedy decode step: append the argmax token and
+ * advance the position, what the standard mode's model.generate does per
+ * token (csaq/inference.py:383). */
 int csaq_greedy_commit(const int64_t* tok, int64_t B, int32_t* pos0, int64_t* out_tokens,
                        int32_t* n_out, int64_t cap, int64_t* next_tok, int32_t* remaining,
                        void* stream);
