@@ -627,20 +627,27 @@ extern "C" int csaq_argmax_parts(const void* logits, int n_parts, int64_t part_s
 
 // ── csaq_decode_attention_static: decode attention with library-owned scratch
 // For callers with no device allocator of their own (see the header). The
-// scratch holds what csaq_decode_attention's `part` and `tickets` hold: the
-// per-chunk partial softmax results (rewritten by every call) and one ticket
-// per (sequence, KV head), which must start at zero and which every completed
-// call leaves at zero.
+// scratch holds what csaq_decode_attention's `part` and `tickets` hold. The
+// tickets (one per sequence and KV head) sit in a fixed region at the start
+// of the array, CSAQ_ATTENTION_STATIC_MAX_HEADS int32 slots that no call's
+// partials reach; they start at zero and every completed call leaves the ones
+// it used at zero, so a call finds its tickets at zero whatever the shape of
+// the call before it. The per-chunk partial softmax results follow at
+// kStaticPartOffset; every call rewrites the ones it reads.
 static __device__ __align__(256) uint8_t g_attn_scratch[CSAQ_ATTENTION_STATIC_SCRATCH_BYTES];
 
 namespace csaq {
 namespace {
 constexpr int kMaxDevices = 64;
+constexpr int64_t kStaticPartOffset = CSAQ_ATTENTION_STATIC_MAX_HEADS * 4;  // bytes; a multiple of 256
+static_assert(kStaticPartOffset % 256 == 0, "partials must stay 256-byte aligned");
 std::mutex g_attn_mu;
 void* g_attn_ptr[kMaxDevices];
 
 // Once per device, with that device current: the buffer's address, zero-filled.
-int attn_scratch(void** out) {
+// The set-up synchronises the device, so it refuses to run while `st` is being
+// captured into a graph (the capture would be invalidated).
+int attn_scratch(cudaStream_t st, void** out) {
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) {
@@ -650,6 +657,13 @@ int attn_scratch(void** out) {
   if (dev < 0 || dev >= kMaxDevices) return CSAQ_ERR_UNSUPPORTED;
   std::lock_guard<std::mutex> lock(g_attn_mu);
   if (!g_attn_ptr[dev]) {
+    cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+    e = cudaStreamIsCapturing(st, &cs);
+    if (e != cudaSuccess) {
+      set_last_cuda_error(e);
+      return CSAQ_ERR_CUDA;
+    }
+    if (cs != cudaStreamCaptureStatusNone) return CSAQ_ERR_UNSUPPORTED;
     void* p = nullptr;
     e = cudaGetSymbolAddress(&p, g_attn_scratch);
     if (e == cudaSuccess) e = cudaMemset(p, 0, CSAQ_ATTENTION_STATIC_SCRATCH_BYTES);
@@ -673,13 +687,13 @@ extern "C" int csaq_decode_attention_static(const void* q, const void* k_cache, 
   if (!q || !k_cache || !v_cache || !pos0 || !out) return CSAQ_ERR_ARG;
   const int64_t floats = csaq_attention_workspace_floats(B, S, Hq, Hkv, D, Lmax);
   if (floats < 0) return CSAQ_ERR_ARG;
-  const int64_t part_bytes = (floats * 4 + 255) / 256 * 256;
-  if (part_bytes + B * Hkv * 4 > CSAQ_ATTENTION_STATIC_SCRATCH_BYTES) return CSAQ_ERR_SCRATCH;
+  if (B * Hkv > CSAQ_ATTENTION_STATIC_MAX_HEADS) return CSAQ_ERR_SCRATCH;
+  if (kStaticPartOffset + floats * 4 > CSAQ_ATTENTION_STATIC_SCRATCH_BYTES) return CSAQ_ERR_SCRATCH;
   void* scratch = nullptr;
-  const int rc = attn_scratch(&scratch);
+  const int rc = attn_scratch(as_stream(stream), &scratch);
   if (rc) return rc;
-  float* part = reinterpret_cast<float*>(scratch);
-  int32_t* tickets = reinterpret_cast<int32_t*>(reinterpret_cast<uint8_t*>(scratch) + part_bytes);
+  int32_t* tickets = reinterpret_cast<int32_t*>(scratch);
+  float* part = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(scratch) + kStaticPartOffset);
   return csaq_decode_attention(q, k_cache, v_cache, pos0, B, S, Hq, Hkv, D, Lmax, scale, part, tickets, out,
                                dtype, stream);
 }

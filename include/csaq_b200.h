@@ -319,14 +319,20 @@ int csaq_argmax_parts(const void* logits, int n_parts, int64_t part_stride, int6
  *
  * Same arguments and results as csaq_decode_attention minus `part` and
  * `tickets`: those live in a fixed CSAQ_ATTENTION_STATIC_SCRATCH_BYTES buffer
- * inside the library, one per device. A call needing more (partials of
- * csaq_attention_workspace_floats floats, 256-byte aligned, then B*Hkv
- * tickets) returns CSAQ_ERR_SCRATCH before anything is enqueued. The first
- * call on each device sets the buffer up (looks up its address and zero-fills
- * it, synchronously); make that first call before any stream capture. Calls
- * on one device share the buffer, so calls that can overlap on the GPU (other
- * streams, other host threads) race; calls ordered on one stream do not. */
+ * inside the library, one per device. The buffer starts with
+ * CSAQ_ATTENTION_STATIC_MAX_HEADS int32 tickets, which every completed call
+ * leaves at zero whatever its shape; the partial softmax results follow. A
+ * call with B*Hkv above CSAQ_ATTENTION_STATIC_MAX_HEADS, or whose partials
+ * (csaq_attention_workspace_floats floats) do not fit after the tickets,
+ * returns CSAQ_ERR_SCRATCH before anything is enqueued. The first call on
+ * each device sets the buffer up (looks up its address and zero-fills it,
+ * synchronously); make that first call before any stream capture (during a
+ * capture it returns CSAQ_ERR_UNSUPPORTED). The set-up is done once per
+ * process: after cudaDeviceReset, reload the library. Calls on one device
+ * share the buffer, so calls that can overlap on the GPU (other streams,
+ * other host threads) race; calls ordered on one stream do not. */
 #define CSAQ_ATTENTION_STATIC_SCRATCH_BYTES (4 << 20)
+#define CSAQ_ATTENTION_STATIC_MAX_HEADS 1024
 int csaq_decode_attention_static(const void* q, const void* k_cache, const void* v_cache,
                                  const int32_t* pos0, int64_t B, int64_t S, int64_t Hq, int64_t Hkv,
                                  int64_t D, int64_t Lmax, float scale, void* out, int dtype, void* stream);
