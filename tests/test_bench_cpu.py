@@ -20,19 +20,23 @@ def _env(**kw):
 
 
 def test_reference_arm_json_line():
+    """The reference's own engine (installed under baseline/_ref) on a tiny decoder."""
     r = subprocess.run(ARGS, capture_output=True, text=True, timeout=600, env=_env(), cwd=REPO)
     assert r.returncode == 0, r.stderr[-2000:]
     lines = [l for l in r.stdout.splitlines() if l.startswith("{")]
     assert len(lines) == 1
     d = json.loads(lines[0])
     assert d["impl"] == "reference"
+    if not os.path.isdir(os.path.join(REPO, "baseline", "_ref", "csaq")):
+        assert "unavailable" in d
+        return
     for key in ("metric", "value", "unit", "n_gpus", "steps", "warmup", "ms_per_step", "higher_is_better",
                 "scaling", "vs_baseline", "dtype", "data", "config", "cpu_baseline", "e2e"):
         assert key in d, key
     assert d["value"] > 0 and d["unit"] == "tokens/s" and d["higher_is_better"] is True
     cb = d["cpu_baseline"]
-    assert cb["kind"] == "port" and cb["cores"] >= 1 and cb["value"] == d["value"]
-    assert "2 layers" in cb["sample"]
+    assert cb["kind"] == "reference" and cb["cores"] >= 1 and cb["value"] == d["value"]
+    assert "CSAQInferenceEngine.generate" in cb["sample"] and "2 layers" in cb["sample"]
     assert d["e2e"] == {"value": d["value"], "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}
     assert d["config"]["workload"].startswith("tiny-llama-shaped decoder")
 
