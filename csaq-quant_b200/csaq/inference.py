@@ -36,11 +36,6 @@ import torch.nn.functional as F
 
 from .kernels import CSAQLinear
 
-try:
-    from transformers.cache_utils import DynamicCache
-except ImportError:  # pragma: no cover
-    DynamicCache = None
-
 
 @dataclass
 class SpeculativeReport:
@@ -172,51 +167,57 @@ class CSAQInferenceEngine:
         if self._in_verify:
             self._swap_to_draft()
 
-    # ── KV cache utilities (csaq/inference.py:241-265) ──────────────────────
+    # ── KV cache utilities (the roles of csaq/inference.py:241-265) ─────────
     @staticmethod
-    def _kv_len(past_key_values: Optional[Any]) -> int:
-        if past_key_values is None:
+    def _kv_len(cache: Optional[Any]) -> int:
+        """Positions a cache holds: 0 for none; a transformers Cache reports
+        its own length, a legacy ((k, v), ...) tuple is read off the first key
+        (batch, heads, positions, head_dim)."""
+        if cache is None:
             return 0
-        if hasattr(past_key_values, "get_seq_length"):
-            return past_key_values.get_seq_length()
-        if hasattr(past_key_values, "key_cache"):
-            kc = past_key_values.key_cache
-            return kc[0].shape[2] if kc else 0
-        return past_key_values[0][0].shape[2]
+        length = getattr(cache, "get_seq_length", None)
+        if length is not None:
+            return int(length())
+        return int(cache[0][0].shape[-2])
 
     @staticmethod
-    def _truncate_kv(past_key_values: Optional[Any], length: int) -> Optional[Any]:
-        if past_key_values is None:
+    def _truncate_kv(cache: Optional[Any], length: int) -> Optional[Any]:
+        """Drop every position from `length` on: in place for a transformers
+        Cache (its crop), as a new tuple for the legacy layout."""
+        if cache is None:
             return None
-        if DynamicCache is not None and isinstance(past_key_values, DynamicCache):
-            if hasattr(past_key_values, "crop"):
-                past_key_values.crop(length)
-                return past_key_values
-            for i in range(len(past_key_values.key_cache)):
-                past_key_values.key_cache[i] = past_key_values.key_cache[i][:, :, :length, :]
-                past_key_values.value_cache[i] = past_key_values.value_cache[i][:, :, :length, :]
-            return past_key_values
-        return tuple(tuple(t[:, :, :length, :] for t in layer) for layer in past_key_values)
+        crop = getattr(cache, "crop", None)
+        if crop is not None:
+            crop(length)
+            return cache
+        return tuple(tuple(t[..., :length, :] for t in layer) for layer in cache)
 
-    # ── sampling (csaq/inference.py:269-304) ────────────────────────────────
+    # ── sampling (the rule of csaq/inference.py:269-304) ────────────────────
     @staticmethod
     def _sample(logits: torch.Tensor, temperature: float, top_p: float,
                 greedy: bool) -> Tuple[torch.Tensor, torch.Tensor]:
-        logits = torch.clamp(logits, -50.0, 50.0)
-        logits = torch.nan_to_num(logits, nan=0.0, posinf=50.0, neginf=-50.0)
+        """One token per row, shape (rows, 1), and the probabilities drawn from.
+
+        NaN logits read as 0 and all are clamped to [-50, 50]. Greedy takes the
+        argmax. Otherwise the logits are divided by the temperature and, for
+        top_p < 1, token j stays in the draw only while the probability mass of
+        the tokens ranked above it is at most top_p (the smallest set whose mass
+        exceeds top_p, ties broken by the sort). Rows whose probabilities are
+        not a usable distribution fall back to the argmax. This is the same rule
+        csaq_sample_rows applies on the device."""
+        z = torch.nan_to_num(logits.float(), nan=0.0).clamp(-50.0, 50.0)
         if greedy:
-            return logits.argmax(dim=-1, keepdim=True), F.softmax(logits, dim=-1)
-        scaled = logits / max(temperature, 1e-8)
+            return z.argmax(-1, keepdim=True), torch.softmax(z, -1)
+        p = torch.softmax(z / max(temperature, 1e-8), -1)
         if top_p < 1.0:
-            sorted_logits, sorted_indices = torch.sort(scaled, descending=True)
-            sp = F.softmax(sorted_logits, dim=-1)
-            remove = torch.cumsum(sp, dim=-1) - sp > top_p
-            sorted_logits[remove] = float("-inf")
-            scaled = torch.zeros_like(logits).scatter(1, sorted_indices, sorted_logits)
-        probs = F.softmax(scaled, dim=-1)
-        if torch.isnan(probs).any() or (probs < 0).any() or probs.sum() < 1e-8:
-            return logits.argmax(dim=-1, keepdim=True), probs
-        return torch.multinomial(probs, 1), probs
+            ranked, order = p.sort(-1, descending=True)
+            above = ranked.cumsum(-1) - ranked
+            keep = torch.zeros_like(p, dtype=torch.bool).scatter_(-1, order, above <= top_p)
+            p = torch.where(keep, p, torch.zeros_like(p))
+            p = p / p.sum(-1, keepdim=True)
+        if not (torch.isfinite(p).all() and bool((p.sum(-1) > 1e-8).all())):
+            return z.argmax(-1, keepdim=True), p
+        return torch.multinomial(p, 1), p
 
     def warmup(self, n: int = 3) -> None:
         if self._warmup_complete:

@@ -2,7 +2,7 @@
 
 Run in the build container (where the reference source tree is present):
 
-    python tests/golden/make_goldens.py [--ref /root/reference] [--full]
+    python tests/golden/make_goldens.py --ref <reference source tree> [--full]
 
 Outputs (committed):
   tests/golden/kernels_golden.npz  quant/pack/dequant/shared-scale/from_cliques cases
@@ -306,7 +306,7 @@ def full_digests(rk, rc, rcfg) -> dict:
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--ref", default="/root/reference")
+    ap.add_argument("--ref", required=True, help="the csaq-quant v0.5.9 source tree (read only)")
     ap.add_argument("--full", action="store_true", help="also compute full-size digests")
     args = ap.parse_args()
     rk, rc, rcfg = _import_reference(args.ref)

@@ -93,7 +93,7 @@ def test_verify_weights_differ_from_draft(tiny_llama):
 
 
 @pytest.mark.parametrize("which,B,K", [("tiny_llama", 1, 4), ("tiny_llama", 3, 4), ("tiny_llama", 2, 2),
-                                       ("tiny_qwen2_d64", 2, 4)])
+                                       ("tiny_llama", 16, 4), ("tiny_qwen2_d64", 2, 4)])
 def test_speculative_equals_greedy_verify(which, B, K, request):
     from csaq.inference import CSAQInferenceEngine
     model, cmap, _ = request.getfixturevalue(which)
