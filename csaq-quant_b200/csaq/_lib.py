@@ -123,6 +123,7 @@ _SIGNATURES = {
     "csaq_tp_exchange_sum": (c_int, [ctypes.POINTER(CsaqP2PGroup), c_i64, c_i64, c_vp, c_i64, c_i64, c_i64, c_int,
                                      c_vp]),
     "csaq_p2p_errors": (c_int, [ctypes.POINTER(CsaqP2PGroup), ctypes.POINTER(c_i64)]),
+    "csaq_p2p_set_spin_limit": (c_int, [c_i64]),
     "csaq_silu_mul": (c_int, [c_vp, c_i64, c_vp, c_i64, c_vp, c_i64, c_i64, c_i64, c_int, c_vp]),
     "csaq_spec_accept": (c_int, [c_vp, c_vp, c_i64, c_i64, c_vp, c_vp, c_vp, c_i64, c_vp, c_vp, c_vp, c_vp, c_vp]),
     "csaq_greedy_commit": (c_int, [c_vp, c_i64, c_vp, c_vp, c_vp, c_i64, c_vp, c_vp, c_vp]),

@@ -162,6 +162,14 @@ def jaccard_cliques(inter: torch.Tensor, f: torch.Tensor, threshold: float) -> L
     return cliques_from_labels(labels)
 
 
+def spearman_rho(ranks: torch.Tensor, prev_ranks: torch.Tensor) -> float:
+    """Spearman's rho of two rank vectors without ties: 1 - 6 sum(d^2) / (n (n^2 - 1))
+    (csaq/core.py:218-222)."""
+    n_r = float(ranks.numel())
+    d = ranks - prev_ranks
+    return 1.0 - (6.0 * (d ** 2).sum().item()) / (n_r * (n_r ** 2 - 1))
+
+
 def cliques_from_labels(labels: torch.Tensor) -> List[List[int]]:
     """Clique lists (ascending members, seed first) from per-channel labels."""
     lab = labels.to(torch.int64).cpu()
@@ -278,19 +286,14 @@ class CausalProfiler:
                         salience_accumulate(acc, g, w)
             self.model.zero_grad()
             if (i + 1) % self._EVAL_STRIDE == 0 and (i + 1) >= self._EARLY_STOP_MIN_BATCHES:
-                all_s = torch.cat([self.salience[n].flatten().to(first_device) for n in self._modules])
-                if world > 1:  # every rank ranks the same (all-reduced) sample, so all stop together
-                    all_s = all_s.clone()
-                    dist.all_reduce(all_s, group=self.dp_group)
                 if eval_idx is None:
-                    size = min(self._SPEARMAN_SAMPLE, all_s.numel())
-                    gen = torch.Generator(device=all_s.device).manual_seed(0)
-                    eval_idx = torch.randperm(all_s.numel(), device=all_s.device, generator=gen)[:size]
-                ranks = all_s[eval_idx].argsort().argsort().float()
+                    eval_idx = self._spearman_indices(first_device, dist, world)
+                sample = self._salience_sample(eval_idx, first_device)
+                if world > 1:  # every rank ranks the same (all-reduced) sample, so all stop together
+                    dist.all_reduce(sample, group=self.dp_group)
+                ranks = sample.argsort().argsort().float()
                 if prev_ranks is not None:
-                    n_r = float(ranks.numel())
-                    d = ranks - prev_ranks
-                    rho = 1.0 - (6.0 * (d ** 2).sum().item()) / (n_r * (n_r ** 2 - 1))
+                    rho = spearman_rho(ranks, prev_ranks)
                     if rho >= self._EARLY_STOP_RHO:
                         if verbose:
                             print(f"[CSAQ] Early stop at batch {i + 1}/{n_samples} (ρ={rho:.4f})")
@@ -310,6 +313,53 @@ class CausalProfiler:
             h.remove()
         self.model.eval()
         return self.salience, self._build_cliques()
+
+    # Sampling without replacement by torch.randperm(N) allocates N indices;
+    # above this many salience entries a chunked sampler is used instead.
+    _RANDPERM_MAX: int = 1 << 26
+
+    def _spearman_indices(self, device, dist, world: int) -> torch.Tensor:
+        """Flat indices (into the layers' salience in module order) of the
+        early-stop sample: torch.randperm(N)[:50000] on the host generator as
+        in csaq/core.py:214-216 while N <= _RANDPERM_MAX; above it, 50000
+        distinct indices drawn uniformly with the host generator (the
+        reference's randperm would allocate N int64 values: 56 GB at the 8B
+        shape). Under data parallelism rank 0 draws and broadcasts."""
+        N = sum(self.salience[n].numel() for n in self._modules)
+        size = min(self._SPEARMAN_SAMPLE, N)
+        if world > 1 and dist.get_rank(self.dp_group) != 0:
+            idx = torch.empty(size, dtype=torch.int64)
+        elif N <= self._RANDPERM_MAX:
+            idx = torch.randperm(N)[:size]
+        else:
+            picked = torch.empty(0, dtype=torch.int64)
+            while picked.numel() < size:
+                cand = torch.randint(0, N, (2 * size,), dtype=torch.int64)
+                picked = torch.cat([picked, cand])
+                # keep the first occurrence of every index, in draw order
+                uniq, inv = torch.unique(picked, return_inverse=True)
+                first = torch.full((uniq.numel(),), picked.numel(), dtype=torch.int64)
+                first.scatter_reduce_(0, inv, torch.arange(picked.numel()), reduce="amin")
+                picked = picked[torch.sort(first).values]
+            idx = picked[:size]
+        if world > 1:
+            idx = idx.to(device)
+            dist.broadcast(idx, 0, group=self.dp_group)
+        return idx.to(device)
+
+    def _salience_sample(self, idx: torch.Tensor, device) -> torch.Tensor:
+        """all_s[idx] for all_s = cat(salience[n].flatten() for n in modules),
+        gathered layer by layer without building all_s."""
+        out = torch.empty(idx.numel(), dtype=torch.float32, device=device)
+        off = 0
+        for n in self._modules:
+            t = self.salience[n]
+            sel = (idx >= off) & (idx < off + t.numel())
+            if bool(sel.any()):
+                loc = (idx[sel] - off).to(t.device)
+                out[sel] = t.reshape(-1)[loc].to(device=device, dtype=torch.float32)
+            off += t.numel()
+        return out
 
     def _build_cliques(self) -> CliqueMap:
         """Partition each layer's output channels (csaq/core.py:240-287)."""

@@ -20,12 +20,15 @@
 // a buffer again only after it has seen every peer's signal for the next
 // exchange, which each peer sends after finishing its reads of this one.
 
+#include <atomic>
+
 #include "common.cuh"
 
 namespace csaq {
 namespace {
 
-constexpr long long kSpinLimit = 1ll << 22;  // polls of a peer flag before giving up (a few seconds)
+constexpr long long kSpinLimit = 1ll << 22;  // default polls of a peer flag before giving up (a few seconds)
+std::atomic<long long> g_spin_limit{kSpinLimit};  // csaq_p2p_set_spin_limit; read at each launch
 
 __device__ __forceinline__ void st_release_sys(uint64_t* p, uint64_t v) {
   asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
@@ -38,7 +41,7 @@ __device__ __forceinline__ uint64_t ld_acquire_sys(const uint64_t* p) {
 
 template <typename T>
 __global__ void tp_exchange_kernel(const csaq_p2p_group G, int64_t part_offset, int64_t ld_p, T* __restrict__ out,
-                                   int64_t ldo, int64_t M, int N) {
+                                   int64_t ldo, int64_t M, int N, long long spin_limit) {
   pdl_wait();  // this rank's partial, written by the previous kernel, is complete
   pdl_trigger();
   __shared__ uint64_t s_seq;
@@ -55,7 +58,7 @@ __global__ void tp_exchange_kernel(const csaq_p2p_group G, int64_t part_offset, 
     const uint64_t* f = G.flags[G.rank] + threadIdx.x;
     long long i = 0;
     while (ld_acquire_sys(f) < want) {
-      if (++i == kSpinLimit) {
+      if (++i == spin_limit) {
         atomicAdd(G.err, 1u);
         break;
       }
@@ -139,11 +142,18 @@ extern "C" int csaq_tp_exchange_sum(const csaq_p2p_group* group, int64_t part_of
   // one wave of CTAs at most, so that every CTA is resident while the others spin
   const int64_t need = (M * N + 255) / 256;
   const unsigned grid = (unsigned)(need < 1 ? 1 : (need > 128 ? 128 : need));
+  const long long spin = g_spin_limit.load();
   if (dtype == CSAQ_DT_BF16)
     return launch_pdl(tp_exchange_kernel<__nv_bfloat16>, dim3(grid), dim3(256), 0, st, G, part_offset, ld_parts,
-                      reinterpret_cast<__nv_bfloat16*>(out), ldo, M, (int)N);
+                      reinterpret_cast<__nv_bfloat16*>(out), ldo, M, (int)N, spin);
   return launch_pdl(tp_exchange_kernel<__half>, dim3(grid), dim3(256), 0, st, G, part_offset, ld_parts,
-                    reinterpret_cast<__half*>(out), ldo, M, (int)N);
+                    reinterpret_cast<__half*>(out), ldo, M, (int)N, spin);
+}
+
+extern "C" int csaq_p2p_set_spin_limit(int64_t polls) {
+  if (polls < 1) return CSAQ_ERR_ARG;
+  g_spin_limit.store(polls);
+  return CSAQ_OK;
 }
 
 extern "C" int csaq_p2p_errors(const csaq_p2p_group* group, int64_t* count) {

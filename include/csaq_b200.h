@@ -302,6 +302,11 @@ int csaq_ipc_close(void* ptr);
 int csaq_tp_exchange_sum(const csaq_p2p_group* group, int64_t part_offset, int64_t ld_parts, void* out,
                          int64_t ldo, int64_t M, int64_t N, int dtype, void* stream);
 int csaq_p2p_errors(const csaq_p2p_group* group, int64_t* count);
+/* Polls of a peer flag before csaq_tp_exchange_sum gives up its wait (default
+ * 2^22, a few seconds), for launches made after the call (a captured graph
+ * keeps the value it was captured with); polls >= 1. No counterpart in the
+ * reference (it has no multi-GPU path). */
+int csaq_p2p_set_spin_limit(int64_t polls);
 
 /* Greedy token of each row: the global index of the largest logit over
  * n_parts vocabulary slices of part_len values (slice r at r*part_stride,

@@ -127,3 +127,66 @@ def test_quantize_export_load_logits_gpu(tmp_path):
     assert got.dtype == ref.dtype
     assert torch.equal(got, ref)
     assert torch.equal(got_v, ref_v)
+
+
+# ── byte identity with the reference's export_csaq_model (uniform-bit layers) ──
+
+def _golden_export():
+    import sys
+    import numpy as np
+    here = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
+    if here not in sys.path:
+        sys.path.insert(0, here)
+    import tiny_nets
+    return np.load(os.path.join(here, "export_golden.npz")), tiny_nets
+
+
+def _export_and_digest(model, tmp_path, tiny_nets):
+    import hashlib
+    from csaq.config import CSAQConfig
+    from csaq.utils import export_csaq_model
+    cfg = CSAQConfig(target_bits=4.0, bit_options=[4, 8], group_size=-1)
+    info = {"causal_map": {"model.layers.0.mlp.down_proj": [1, 5, 9]}, "tier_stats": {"int4": 1234},
+            "actual_bits": 4.0, "cliques_count": 7}
+    d = str(tmp_path / "export")
+    export_csaq_model(model, cfg, tiny_nets.uniform_budget(model, 4), d, info)
+    out = {}
+    for f in ("config.json", "csaq_manifest.json", "model.safetensors", "tokenizer_config.json"):
+        with open(os.path.join(d, f), "rb") as fh:
+            out[f] = hashlib.sha256(fh.read()).digest()
+    return out
+
+
+def test_uniform_export_byte_identical_to_reference(tmp_path):
+    """A uniform 4-bit model with the reference's own quantised buffers exports
+    config.json, csaq_manifest.json, model.safetensors and tokenizer_config.json
+    byte for byte as the reference's export_csaq_model (csaq/utils.py:225-318)."""
+    from csaq.kernels import CSAQLinear
+    g, tiny_nets = _golden_export()
+    model = tiny_nets.tiny_llama()
+    for name, lin in list(model.named_modules()):
+        if isinstance(lin, nn.Linear) and "lm_head" not in name:
+            parent_name, _, child = name.rpartition(".")
+            setattr(model.get_submodule(parent_name), child,
+                    CSAQLinear(lin.in_features, lin.out_features, 4, bias=lin.bias, group_size=-1))
+    state = {k[2:]: torch.from_numpy(g[k]) for k in g.files if k.startswith("q_")}
+    model.load_state_dict(state, strict=True)
+    got = _export_and_digest(model, tmp_path, tiny_nets)
+    for f, dig in got.items():
+        assert dig == g[f"sha_{f}"].tobytes(), f
+
+
+@pytest.mark.gpu
+def test_uniform_export_from_our_quantiser_byte_identical(tmp_path):
+    """The same tiny Llama quantised by this package's inject_csaq_linear (GPU
+    kernels) exports the reference's bytes."""
+    from csaq.kernels import inject_csaq_linear
+    g, tiny_nets = _golden_export()
+    model = tiny_nets.tiny_llama()
+    for k, v in model.state_dict().items():
+        assert torch.equal(v, torch.from_numpy(g[f"w_{k}"])), k
+    model = model.cuda()
+    inject_csaq_linear(model, tiny_nets.uniform_budget(model, 4), verbose=False)
+    got = _export_and_digest(model, tmp_path, tiny_nets)
+    for f, dig in got.items():
+        assert dig == g[f"sha_{f}"].tobytes(), f
