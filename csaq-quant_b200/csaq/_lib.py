@@ -107,6 +107,9 @@ _SIGNATURES = {
     "csaq_attention_workspace_floats": (c_i64, [c_i64, c_i64, c_i64, c_i64, c_i64, c_i64]),
     "csaq_decode_attention": (c_int, [c_vp, c_vp, c_vp, c_vp, c_i64, c_i64, c_i64, c_i64, c_i64, c_i64,
                                       ctypes.c_float, c_vp, c_vp, c_vp, c_int, c_vp]),
+    "csaq_decode_attention_rope": (c_int, [c_vp, c_vp, c_vp, c_i64, c_vp, c_i64, c_i64, c_i64, c_i64, c_i64,
+                                           c_vp, c_vp, c_vp, c_vp, c_i64, ctypes.c_float, c_vp, c_vp, c_vp,
+                                           c_int, c_vp]),
     "csaq_decode_attention_static": (c_int, [c_vp, c_vp, c_vp, c_vp, c_i64, c_i64, c_i64, c_i64, c_i64, c_i64,
                                              ctypes.c_float, c_vp, c_int, c_vp]),
     "csaq_rank_sum": (c_int, [c_vp, c_int, c_i64, c_i64, c_vp, c_i64, c_i64, c_i64, c_int, c_int, c_vp]),

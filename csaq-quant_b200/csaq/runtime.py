@@ -5,8 +5,8 @@ kernels over preallocated buffers, so a whole decode step (or a whole
 self-speculative block: K draft steps, one verify pass over K+1 tokens and
 the on-device acceptance) is captured once as a CUDA graph and replayed:
 
-    RMSNorm -> fused q/k/v quantised GEMV -> RoPE + KV-cache write ->
-    split-K decode attention -> o_proj GEMV (+ residual) -> RMSNorm ->
+    RMSNorm -> fused q/k/v quantised GEMV -> RoPE + KV-cache write +
+    split-K decode attention (one launch) -> o_proj GEMV (+ residual) -> RMSNorm ->
     fused gate/up GEMV -> SiLU gate -> down GEMV (+ residual)
 
 The unquantised lm_head runs as an fp16 tier of the same GEMV kernel (every
@@ -366,11 +366,18 @@ class DecodeRuntime:
 
     def _attention(self, li: int, sh: "_Shape", S: int, pos: torch.Tensor, pos_host: Optional[int],
                    scale: float, st: int) -> None:
-        """Attention of the step's queries over the cache. Prefill chunks of
-        PREFILL_SDPA_TOKENS tokens or more (all sequences at the same host-known
-        start) go to torch's fused scaled-dot-product attention; decode and
-        verify steps to the split-key decode kernel."""
+        """RoPE, the KV-cache write and attention of the step's queries over the
+        cache. Prefill chunks of PREFILL_SDPA_TOKENS tokens or more (all
+        sequences at the same host-known start) go to csaq_rope_kv and torch's
+        fused scaled-dot-product attention; decode and verify steps to the
+        split-key decode kernel with the rotation fused in."""
+        qkv, nq, nkv = sh.qkv, self.Hq_l * self.D, self.Hkv_l * self.D
         if pos_host is not None and S >= PREFILL_SDPA_TOKENS:
+            check(lib().csaq_rope_kv(qkv.data_ptr(), qkv.stride(0), qkv[:, nq:].data_ptr(), qkv.stride(0),
+                                     qkv[:, nq + nkv:].data_ptr(), qkv.stride(0), pos.data_ptr(), self.B, S,
+                                     self.Hq_l, self.Hkv_l, self.D, self.cos.data_ptr(), self.sin.data_ptr(),
+                                     sh.q_rot.data_ptr(), self.k_cache[li].data_ptr(),
+                                     self.v_cache[li].data_ptr(), self.Lmax, self.dt, st), "rope_kv")
             B, Hq, Hkv, D = self.B, self.Hq_l, self.Hkv_l, self.D
             n = pos_host + S
             q = sh.q_rot.view(B, S, Hq, D).transpose(1, 2)
@@ -384,11 +391,13 @@ class DecodeRuntime:
                 o = F.scaled_dot_product_attention(q, k, v, attn_mask=mask, scale=scale, enable_gqa=Hq != Hkv)
             sh.attn.view(B, S, Hq, D).copy_(o.transpose(1, 2))
             return
-        check(lib().csaq_decode_attention(sh.q_rot.data_ptr(), self.k_cache[li].data_ptr(),
-                                          self.v_cache[li].data_ptr(), pos.data_ptr(), self.B, S, self.Hq_l,
-                                          self.Hkv_l, self.D, self.Lmax, scale, sh.part.data_ptr(),
-                                          self.tickets[li].data_ptr(), sh.attn.data_ptr(), self.dt, st),
-              "attention")
+        # decode / verify / short chunks: RoPE, the cache write and attention in one launch
+        check(lib().csaq_decode_attention_rope(qkv.data_ptr(), qkv[:, nq:].data_ptr(), qkv[:, nq + nkv:].data_ptr(),
+                                               qkv.stride(0), pos.data_ptr(), self.B, S, self.Hq_l, self.Hkv_l,
+                                               self.D, self.cos.data_ptr(), self.sin.data_ptr(),
+                                               self.k_cache[li].data_ptr(), self.v_cache[li].data_ptr(), self.Lmax,
+                                               scale, sh.part.data_ptr(), self.tickets[li].data_ptr(),
+                                               sh.attn.data_ptr(), self.dt, st), "attention")
 
     @torch.no_grad()
     def step(self, S: int, ids: torch.Tensor, pos: torch.Tensor, verify: bool,
@@ -410,12 +419,6 @@ class DecodeRuntime:
             check(L.csaq_rmsnorm(sh.x.data_ptr(), H, layer.input_layernorm.weight.data_ptr(),
                                  sh.xn.data_ptr(), H, M, H, self.eps, self.dt, st), "rmsnorm")
             self._gemv(sh.descs[(li, "qkv", verify)], H, sh.xn, M, st)
-            qkv = sh.qkv
-            check(L.csaq_rope_kv(qkv.data_ptr(), qkv.stride(0), qkv[:, nq:].data_ptr(), qkv.stride(0),
-                                 qkv[:, nq + nkv:].data_ptr(), qkv.stride(0), pos.data_ptr(), self.B, S,
-                                 Hq, Hkv, D, self.cos.data_ptr(), self.sin.data_ptr(),
-                                 sh.q_rot.data_ptr(), self.k_cache[li].data_ptr(),
-                                 self.v_cache[li].data_ptr(), self.Lmax, self.dt, st), "rope_kv")
             self._attention(li, sh, S, pos, pos_host, scale, st)
             self._gemv(sh.descs[(li, "o", verify)], nq, sh.attn, M, st)
             if self.tp > 1:
@@ -469,10 +472,10 @@ class DecodeRuntime:
 
     def kernels_per_step(self, S: int) -> int:
         """Own (libcsaq) kernel launches in one step of up to 16 tokens per
-        GEMV launch: per layer 2 RMSNorm, 4 GEMV, RoPE, attention, SiLU (and
-        2 rank-order combines under TP); plus the final RMSNorm, the lm_head
-        GEMV and the argmax."""
-        return self.n_layers * (9 + (2 if self.tp > 1 else 0)) + 3
+        GEMV launch: per layer 2 RMSNorm, 4 GEMV, RoPE with attention (one
+        launch), SiLU (and 2 rank-order combines under TP); plus the final
+        RMSNorm, the lm_head GEMV and the argmax."""
+        return self.n_layers * (8 + (2 if self.tp > 1 else 0)) + 3
 
     def prefill_kernels(self, P: int, verify: bool = True) -> int:
         """Own kernel launches of reset() for a P-token prompt: per chunk and
@@ -493,7 +496,7 @@ class DecodeRuntime:
                         n += sum(1 for i in range(nd) if arr[i].n_rows > 0)
                     else:
                         n += -(-M // 16)
-                n += 4 + (0 if S >= PREFILL_SDPA_TOKENS else 1) + (2 if self.tp > 1 else 0)
+                n += 4 + (2 if self.tp > 1 else 0)  # 2 RMSNorm, SiLU, RoPE (+ SDPA) or fused RoPE + attention
             n += 2
         return n + 1
 

@@ -193,15 +193,67 @@ __device__ __forceinline__ void cp_async_commit_wait_all() {
 // (max, sum, o[D]) per row, and the last CTA of (bh) to finish (atomic ticket,
 // no waiting) merges the partials and writes the output. The ticket counter
 // is reset by that CTA, so the workspace needs zeroing only once.
+// The CTA stages its query rows in shared memory (dynamic, R x D) with one
+// round trip, so the per-row loops below start without a global load, and the
+// merge issues its partial loads in batches (no branch on loaded values).
 constexpr int kChunk = 64;
-constexpr int kAttnWarps = 4;
+constexpr int kAttnWarps = 16;
+constexpr int kMergeBatch = 16;  // partials whose loads are issued together in the merge
+constexpr int kKeyBlock = 8;     // keys scored together: independent dot products, one shuffle tree
 
+// ROPE: the launch also does csaq_rope_kv's work for the step's tokens (same
+// expressions, so the same bits): q holds the unrotated queries (rows ldq
+// apart), every CTA rotates its own query rows into shared memory, and the CTA
+// whose chunk holds a new position rotates that key and copies its value from
+// knew / vnew (rows ldq apart) into shared memory and into the cache.
+struct RopeArgs {
+  const void* knew;
+  const void* vnew;
+  int64_t ldq;
+  const float* cos_t;
+  const float* sin_t;
+};
+
+// csaq_rope_kv's rotation of 8 pairs (x[i0..i0+8), x[i0+D/2..i0+D/2+8)) at `pos`
 template <typename T, int D>
+__device__ __forceinline__ void rope8(const T* src, int i0, const float* cos_t, const float* sin_t, int pos,
+                                      uint4& lo, uint4& hi) {
+  constexpr int half = D / 2;
+  const uint4 a = *reinterpret_cast<const uint4*>(src + i0);
+  const uint4 c = *reinterpret_cast<const uint4*>(src + i0 + half);
+  const float* cs = cos_t + (int64_t)pos * D;
+  const float* sn = sin_t + (int64_t)pos * D;
+  float ca[8], sa[8], cb[8], sb[8];
+#pragma unroll
+  for (int t = 0; t < 2; ++t) {
+    const float4 c0 = reinterpret_cast<const float4*>(cs + i0)[t];
+    const float4 s0 = reinterpret_cast<const float4*>(sn + i0)[t];
+    const float4 c1 = reinterpret_cast<const float4*>(cs + i0 + half)[t];
+    const float4 s1 = reinterpret_cast<const float4*>(sn + i0 + half)[t];
+    ca[4 * t] = c0.x; ca[4 * t + 1] = c0.y; ca[4 * t + 2] = c0.z; ca[4 * t + 3] = c0.w;
+    sa[4 * t] = s0.x; sa[4 * t + 1] = s0.y; sa[4 * t + 2] = s0.z; sa[4 * t + 3] = s0.w;
+    cb[4 * t] = c1.x; cb[4 * t + 1] = c1.y; cb[4 * t + 2] = c1.z; cb[4 * t + 3] = c1.w;
+    sb[4 * t] = s1.x; sb[4 * t + 1] = s1.y; sb[4 * t + 2] = s1.z; sb[4 * t + 3] = s1.w;
+  }
+  const T* ae = reinterpret_cast<const T*>(&a);
+  const T* ce = reinterpret_cast<const T*>(&c);
+  T* le = reinterpret_cast<T*>(&lo);
+  T* he = reinterpret_cast<T*>(&hi);
+#pragma unroll
+  for (int t = 0; t < 8; ++t) {
+    const float x0 = to_f32<T>(ae[t]), x1 = to_f32<T>(ce[t]);
+    le[t] = from_f32<T>(fmaf(x0, ca[t], -x1 * sa[t]));
+    he[t] = from_f32<T>(fmaf(x1, cb[t], x0 * sb[t]));
+  }
+}
+
+template <typename T, int D, bool ROPE>
 __global__ void __launch_bounds__(kAttnWarps * 32) attention_kernel(
-    const T* __restrict__ q, const T* __restrict__ k_cache, const T* __restrict__ v_cache,
+    const T* __restrict__ q, T* __restrict__ k_cache, T* __restrict__ v_cache,
     const int32_t* __restrict__ pos0, int S, int Hq, int Hkv, int Lmax, float scale,
-    float* __restrict__ part, int32_t* __restrict__ tickets, T* __restrict__ out) {
+    float* __restrict__ part, int32_t* __restrict__ tickets, T* __restrict__ out, const RopeArgs ra) {
   constexpr int E = D / 32;  // head elements per lane
+  constexpr int half = D / 2, gpr = half / 8;
   const int bh = blockIdx.x, sp = blockIdx.y, n_split = gridDim.y;
   const int b = bh / Hkv, h = bh % Hkv;
   const int G = Hq / Hkv, R = S * G;
@@ -218,6 +270,8 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attention_kernel(
   const int k0 = sp * kChunk;
   __shared__ __align__(16) T ks[kChunk][D];
   __shared__ __align__(16) T vs[kChunk][D];
+  extern __shared__ __align__(16) uint8_t attn_dyn[];
+  T* qs = reinterpret_cast<T*>(attn_dyn);  // [R][D] the (rotated) query rows, unscaled
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int n_keys = max(0, min(kChunk, len - k0));
   const int n_old = max(0, min(n_keys, p0 - k0));
@@ -229,30 +283,71 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attention_kernel(
   }
   pdl_wait();
   pdl_trigger();
-  for (int e = n_old * D / 8 + threadIdx.x; e < n_keys * D / 8; e += blockDim.x) {
-    cp_async16(reinterpret_cast<uint4*>(&ks[0][0]) + e, reinterpret_cast<const uint4*>(kb) + e);
-    cp_async16(reinterpret_cast<uint4*>(&vs[0][0]) + e, reinterpret_cast<const uint4*>(vb) + e);
+  if constexpr (ROPE) {
+    // the chunk's new positions: rotated keys and copied values, into shared
+    // memory and the cache (work items as csaq_rope_kv: 8 rotary pairs, or one
+    // 16-byte value vector); then the query rows, rotated
+    const int n_new = n_keys - n_old;
+    for (int w = threadIdx.x; w < n_new * (gpr + D / 8); w += blockDim.x) {
+      const int j = n_old + w / (gpr + D / 8), item = w % (gpr + D / 8);
+      const int pos = k0 + j;
+      const int64_t m = (int64_t)b * S + (pos - p0);  // token row of the step
+      if (item < gpr) {
+        const int i0 = item * 8;
+        uint4 lo, hi;
+        rope8<T, D>(reinterpret_cast<const T*>(ra.knew) + m * ra.ldq + (int64_t)h * D, i0, ra.cos_t, ra.sin_t, pos,
+                    lo, hi);
+        T* kc = k_cache + (((int64_t)b * Hkv + h) * Lmax + pos) * D;
+        *reinterpret_cast<uint4*>(&ks[j][i0]) = lo;
+        *reinterpret_cast<uint4*>(&ks[j][i0 + half]) = hi;
+        *reinterpret_cast<uint4*>(kc + i0) = lo;
+        *reinterpret_cast<uint4*>(kc + i0 + half) = hi;
+      } else {
+        const int i0 = (item - gpr) * 8;
+        const uint4 v4 =
+            *reinterpret_cast<const uint4*>(reinterpret_cast<const T*>(ra.vnew) + m * ra.ldq + (int64_t)h * D + i0);
+        *reinterpret_cast<uint4*>(&vs[j][i0]) = v4;
+        *reinterpret_cast<uint4*>(v_cache + (((int64_t)b * Hkv + h) * Lmax + pos) * D + i0) = v4;
+      }
+    }
+    for (int w = threadIdx.x; w < R * gpr; w += blockDim.x) {
+      const int r = w / gpr, i0 = (w % gpr) * 8;
+      const int s = r / G, hq = h * G + r % G;
+      uint4 lo, hi;
+      rope8<T, D>(q + ((int64_t)b * S + s) * ra.ldq + (int64_t)hq * D, i0, ra.cos_t, ra.sin_t, p0 + s, lo, hi);
+      *reinterpret_cast<uint4*>(qs + (int64_t)r * D + i0) = lo;
+      *reinterpret_cast<uint4*>(qs + (int64_t)r * D + i0 + half) = hi;
+    }
+  } else {
+    for (int e = n_old * D / 8 + threadIdx.x; e < n_keys * D / 8; e += blockDim.x) {
+      cp_async16(reinterpret_cast<uint4*>(&ks[0][0]) + e, reinterpret_cast<const uint4*>(kb) + e);
+      cp_async16(reinterpret_cast<uint4*>(&vs[0][0]) + e, reinterpret_cast<const uint4*>(vb) + e);
+    }
+    for (int e = threadIdx.x; e < R * (D / 8); e += blockDim.x) {
+      const int r = e / (D / 8), i0 = (e % (D / 8)) * 8;
+      const int s = r / G, hq = h * G + r % G;
+      cp_async16(qs + (int64_t)r * D + i0, q + (((int64_t)b * S + s) * Hq + hq) * D + i0);
+    }
   }
   cp_async_commit_wait_all();
   __syncthreads();
   // partial layout: [bh][sp][r][D + 2]
   float* pbase = part + ((int64_t)bh * n_split + sp) * R * (D + 2);
   for (int r = warp; r < R; r += kAttnWarps) {
-    const int s = r / G, hq = h * G + r % G;
-    const int qpos = pos0[b] + s;  // attends keys 0..qpos
-    const T* qr = q + (((int64_t)b * S + s) * Hq + hq) * D;
+    const int s = r / G;
+    const int qpos = p0 + s;  // attends keys 0..qpos
     float qv[E];
 #pragma unroll
-    for (int i = 0; i < E; ++i) qv[i] = to_f32<T>(qr[lane * E + i]) * scale;
+    for (int i = 0; i < E; ++i) qv[i] = to_f32<T>(qs[(int64_t)r * D + lane * E + i]) * scale;
     const int kmax = min(n_keys, qpos - k0 + 1);
     float m = -INFINITY, l = 0.0f, o[E];
 #pragma unroll
     for (int i = 0; i < E; ++i) o[i] = 0.0f;
     int j = 0;
-    for (; j + 4 <= kmax; j += 4) {  // four keys per step: independent dot products
-      float d[4];
+    for (; j + kKeyBlock <= kmax; j += kKeyBlock) {  // a block of keys: independent dot products
+      float d[kKeyBlock];
 #pragma unroll
-      for (int t = 0; t < 4; ++t) {
+      for (int t = 0; t < kKeyBlock; ++t) {
         d[t] = 0.0f;
 #pragma unroll
         for (int i = 0; i < E; ++i) d[t] = fmaf(qv[i], to_f32<T>(ks[j + t][lane * E + i]), d[t]);
@@ -260,18 +355,23 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attention_kernel(
 #pragma unroll
       for (int off = 16; off > 0; off >>= 1)
 #pragma unroll
-        for (int t = 0; t < 4; ++t) d[t] += __shfl_xor_sync(0xffffffffu, d[t], off);
-      const float mn = fmaxf(fmaxf(m, fmaxf(d[0], d[1])), fmaxf(d[2], d[3]));
-      const float corr = __expf(m - mn);
-      float p[4];
+        for (int t = 0; t < kKeyBlock; ++t) d[t] += __shfl_xor_sync(0xffffffffu, d[t], off);
+      float mn = m;
 #pragma unroll
-      for (int t = 0; t < 4; ++t) p[t] = __expf(d[t] - mn);
-      l = fmaf(l, corr, (p[0] + p[1]) + (p[2] + p[3]));
+      for (int t = 0; t < kKeyBlock; ++t) mn = fmaxf(mn, d[t]);
+      const float corr = __expf(m - mn);
+      float p[kKeyBlock], ps = 0.0f;
+#pragma unroll
+      for (int t = 0; t < kKeyBlock; ++t) {
+        p[t] = __expf(d[t] - mn);
+        ps += p[t];
+      }
+      l = fmaf(l, corr, ps);
 #pragma unroll
       for (int i = 0; i < E; ++i) {
         float acc = o[i] * corr;
 #pragma unroll
-        for (int t = 0; t < 4; ++t) acc = fmaf(p[t], to_f32<T>(vs[j + t][lane * E + i]), acc);
+        for (int t = 0; t < kKeyBlock; ++t) acc = fmaf(p[t], to_f32<T>(vs[j + t][lane * E + i]), acc);
         o[i] = acc;
       }
       m = mn;
@@ -301,24 +401,39 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attention_kernel(
   __syncthreads();
   if (!is_last) return;
   __threadfence();
+  // merge, in chunk order: an empty chunk left m = -inf, l = 0, o = 0, whose
+  // weight exp(-inf - M) is 0, so every chunk is added without a branch on the
+  // loaded values and the loads of a batch go out together
   for (int r = warp; r < R; r += kAttnWarps) {
     const int s = r / G, hq = h * G + r % G;
-    float M_ = -INFINITY;
-#pragma unroll 8
-    for (int p = 0; p < n_split; ++p)
-      M_ = fmaxf(M_, __ldcg(part + (((int64_t)bh * n_split + p) * R + r) * (D + 2) + D));
+    const float* prow = part + ((int64_t)bh * n_split * R + r) * (D + 2);  // chunk p at + p * R * (D + 2)
+    const int64_t pstride = (int64_t)R * (D + 2);
+    float M_ = -INFINITY;  // the maxima, lane-parallel (a maximum is exact in any order)
+    for (int p = lane; p < n_split; p += 32) M_ = fmaxf(M_, __ldcg(prow + p * pstride + D));
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) M_ = fmaxf(M_, __shfl_xor_sync(0xffffffffu, M_, off));
     float L = 0.0f, o[E];
 #pragma unroll
     for (int i = 0; i < E; ++i) o[i] = 0.0f;
-#pragma unroll 4
-    for (int p = 0; p < n_split; ++p) {
-      const float* pr = part + (((int64_t)bh * n_split + p) * R + r) * (D + 2);
-      const float mp = __ldcg(pr + D);
-      if (mp == -INFINITY) continue;
-      const float w = __expf(mp - M_);
-      L = fmaf(__ldcg(pr + D + 1), w, L);
+    for (int p0b = 0; p0b < n_split; p0b += kMergeBatch) {
+      float mb[kMergeBatch], lb[kMergeBatch], ob[kMergeBatch][E];
 #pragma unroll
-      for (int i = 0; i < E; ++i) o[i] = fmaf(__ldcg(pr + lane * E + i), w, o[i]);
+      for (int u = 0; u < kMergeBatch; ++u) {
+        const bool ok = p0b + u < n_split;
+        const float* pr = prow + (p0b + u) * pstride;
+        mb[u] = ok ? __ldcg(pr + D) : -INFINITY;
+        lb[u] = ok ? __ldcg(pr + D + 1) : 0.0f;
+#pragma unroll
+        for (int i = 0; i < E; ++i) ob[u][i] = ok ? __ldcg(pr + lane * E + i) : 0.0f;
+      }
+#pragma unroll
+      for (int u = 0; u < kMergeBatch; ++u) {
+        if (p0b + u >= n_split) break;
+        const float w = __expf(mb[u] - M_);
+        L = fmaf(lb[u], w, L);
+#pragma unroll
+        for (int i = 0; i < E; ++i) o[i] = fmaf(ob[u][i], w, o[i]);
+      }
     }
     T* orow = out + (((int64_t)b * S + s) * Hq + hq) * D;
     const float inv = L > 0.0f ? 1.0f / L : 0.0f;
@@ -539,13 +654,32 @@ extern "C" int64_t csaq_attention_workspace_floats(int64_t B, int64_t S, int64_t
   return B * Hkv * n_split * S * (Hq / Hkv) * (D + 2);
 }
 
-template <typename T>
+// dynamic shared memory of the staged query rows, at least kAttnSpreadBytes:
+// with the static K/V tiles that is more than half an SM's shared memory, so
+// the CTAs of a launch land on distinct SMs even when the launch starts while
+// the previous kernel still holds most of them (an SM freed early would
+// otherwise take several CTAs, which then share its issue slots)
+constexpr int kAttnQBytesMax = 160 * 1024;
+constexpr int kAttnSpreadBytes = 96 * 1024;
+
+template <typename T, bool ROPE = false>
 static int launch_attention(int64_t D, dim3 grid, cudaStream_t st, const void* q, const void* k_cache,
                             const void* v_cache, const int32_t* pos0, int64_t S, int64_t Hq, int64_t Hkv,
-                            int64_t Lmax, float scale, float* part, int32_t* tickets, void* out) {
-  auto kern = D == 64 ? attention_kernel<T, 64> : attention_kernel<T, 128>;
-  return launch_pdl(kern, grid, dim3(kAttnWarps * 32), 0, st, (const T*)q, (const T*)k_cache, (const T*)v_cache,
-                    pos0, (int)S, (int)Hq, (int)Hkv, (int)Lmax, scale, part, tickets, (T*)out);
+                            int64_t Lmax, float scale, float* part, int32_t* tickets, void* out,
+                            const RopeArgs& ra = RopeArgs{}) {
+  auto kern = D == 64 ? attention_kernel<T, 64, ROPE> : attention_kernel<T, 128, ROPE>;
+  int64_t qbytes = S * (Hq / Hkv) * D * (int64_t)sizeof(T);
+  if (qbytes > kAttnQBytesMax) return CSAQ_ERR_UNSUPPORTED;
+  qbytes = qbytes > kAttnSpreadBytes ? qbytes : kAttnSpreadBytes;
+  static bool opted[2] = {false, false};
+  bool& done = opted[D == 64 ? 0 : 1];
+  if (!done) {
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kAttnQBytesMax) != cudaSuccess)
+      return launch_status();
+    done = true;
+  }
+  return launch_pdl(kern, grid, dim3(kAttnWarps * 32), (size_t)qbytes, st, (const T*)q, (T*)k_cache, (T*)v_cache,
+                    pos0, (int)S, (int)Hq, (int)Hkv, (int)Lmax, scale, part, tickets, (T*)out, ra);
 }
 
 extern "C" int csaq_decode_attention(const void* q, const void* k_cache, const void* v_cache,
@@ -563,6 +697,29 @@ extern "C" int csaq_decode_attention(const void* q, const void* k_cache, const v
                                            tickets, out);
   return launch_attention<__half>(D, grid, st, q, k_cache, v_cache, pos0, S, Hq, Hkv, Lmax, scale, part, tickets,
                                   out);
+}
+
+extern "C" int csaq_decode_attention_rope(const void* q, const void* k, const void* v, int64_t ld,
+                                          const int32_t* pos0, int64_t B, int64_t S, int64_t Hq, int64_t Hkv,
+                                          int64_t D, const float* cos_t, const float* sin_t, void* k_cache,
+                                          void* v_cache, int64_t Lmax, float scale, float* part, int32_t* tickets,
+                                          void* out, int dtype, void* stream) {
+  if (!q || !k || !v || !pos0 || !cos_t || !sin_t || !k_cache || !v_cache || !part || !tickets || !out)
+    return CSAQ_ERR_ARG;
+  if (D != 128 && D != 64) return CSAQ_ERR_UNSUPPORTED;
+  if (B <= 0 || S <= 0 || Hq <= 0 || Hkv <= 0 || Hq % Hkv || Lmax <= 0 || ld < Hq * D) return CSAQ_ERR_ARG;
+  if (dtype != CSAQ_DT_F16 && dtype != CSAQ_DT_BF16) return CSAQ_ERR_ARG;
+  auto a16 = [](const void* p) { return reinterpret_cast<uintptr_t>(p) % 16 == 0; };
+  if (ld % 8 || !a16(q) || !a16(k) || !a16(v) || !a16(k_cache) || !a16(v_cache) || !a16(cos_t) || !a16(sin_t))
+    return CSAQ_ERR_UNSUPPORTED;
+  const dim3 grid((unsigned)(B * Hkv), (unsigned)((Lmax + kChunk - 1) / kChunk));
+  cudaStream_t st = as_stream(stream);
+  const RopeArgs ra{k, v, ld, cos_t, sin_t};
+  if (dtype == CSAQ_DT_BF16)
+    return launch_attention<__nv_bfloat16, true>(D, grid, st, q, k_cache, v_cache, pos0, S, Hq, Hkv, Lmax, scale,
+                                                 part, tickets, out, ra);
+  return launch_attention<__half, true>(D, grid, st, q, k_cache, v_cache, pos0, S, Hq, Hkv, Lmax, scale, part,
+                                        tickets, out, ra);
 }
 
 extern "C" int csaq_silu_mul(const void* g, int64_t ldg, const void* u, int64_t ldu, void* h,

@@ -315,6 +315,20 @@ int csaq_p2p_set_spin_limit(int64_t polls);
 int csaq_argmax_parts(const void* logits, int n_parts, int64_t part_stride, int64_t ld, int64_t part_len,
                       int64_t M, int64_t* idx, int dtype, void* stream);
 
+/* csaq_rope_kv followed by csaq_decode_attention in one launch, bit for bit:
+ * q, k, v are the step's unrotated queries and keys and its values, rows `ld`
+ * elements apart (row slices of one fused q/k/v buffer); the new keys are
+ * rotated and, with the values, written to the caches at positions
+ * pos0[b] .. pos0[b]+S-1; the queries are rotated in registers (no rotated
+ * copy is written). Same part/tickets contract as csaq_decode_attention.
+ * Needs 16-byte aligned q/k/v/caches/tables and ld % 8 == 0 (else
+ * CSAQ_ERR_UNSUPPORTED). No counterpart in the reference (HF applies the
+ * rotary embedding and attention as separate ops, csaq/inference.py:443-474). */
+int csaq_decode_attention_rope(const void* q, const void* k, const void* v, int64_t ld, const int32_t* pos0,
+                               int64_t B, int64_t S, int64_t Hq, int64_t Hkv, int64_t D, const float* cos_t,
+                               const float* sin_t, void* k_cache, void* v_cache, int64_t Lmax, float scale,
+                               float* part, int32_t* tickets, void* out, int dtype, void* stream);
+
 /* csaq_decode_attention for callers that cannot allocate device memory: a
  * host-language binding that is handed raw device pointers (q, the caches,
  * pos0, out) by an application owning all device memory, or a

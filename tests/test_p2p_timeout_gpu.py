@@ -30,7 +30,7 @@ def _exchange(G, out, N, M):
 def test_tp_exchange_wait_runs_out_and_returns():
     from csaq import _lib
     from csaq._lib import check, lib
-    M, N = 2, 256
+    M, N = 1, 256  # one CTA: each CTA of the exchange waits (and gives up) on its own
     g = torch.Generator().manual_seed(3)
     parts = [torch.randn(M, N, generator=g).to(torch.bfloat16).to(DEV) for _ in range(2)]
     flags = [torch.zeros(2, dtype=torch.int64, device=DEV) for _ in range(2)]  # flags[0][1]: never written

@@ -17,6 +17,16 @@ import torch
 pytestmark = pytest.mark.gpu
 
 
+def _np(obj):
+    """Tensors -> numpy arrays, recursively: a tensor on a multiprocessing queue
+    is a shared-memory handle that dies with the worker process."""
+    if isinstance(obj, torch.Tensor):
+        return obj.detach().float().cpu().numpy() if obj.is_floating_point() else obj.detach().cpu().numpy()
+    if isinstance(obj, dict):
+        return {k: _np(v) for k, v in obj.items()}
+    return obj
+
+
 def _free_port():
     with socket.socket() as s:
         s.bind(("127.0.0.1", 0))
@@ -77,7 +87,7 @@ def _worker(rank, world, port, q):
             one.reset(prompt, 8, verify=True)
             out["tp1_logits"] = one.prefill_logits.float().cpu()
         dist.barrier()
-        q.put((rank, out))
+        q.put((rank, _np(out)))
     finally:
         dist.destroy_process_group()
 
@@ -101,8 +111,8 @@ def test_tensor_parallel_runtime_two_gpus():
         assert res[r]["peer_memory"], r
         assert res[r]["p2p_errors"] == 0, r
         assert res[r]["nccl_logits_equal"] and res[r]["nccl_greedy_equal"], r
-    a, b = res[0]["tp_logits"], res[0]["tp1_logits"]
-    assert torch.equal(res[0]["tp_logits"], res[1]["tp_logits"])
+    a, b = torch.from_numpy(res[0]["tp_logits"]), torch.from_numpy(res[0]["tp1_logits"])
+    assert torch.equal(torch.from_numpy(res[0]["tp_logits"]), torch.from_numpy(res[1]["tp_logits"]))
     err = float((a - b).norm() / b.norm())
     cos = float(torch.nn.functional.cosine_similarity(a.flatten(), b.flatten(), dim=0))
     assert err < 3e-2 and cos > 0.999, (err, cos)
@@ -131,7 +141,7 @@ def _dp_worker(rank, world, port, q):
             sal1, cl1 = CausalProfiler(model, cfg).profile(calib, verbose=False)
             out["sal1"] = {k: v.cpu() for k, v in sal1.items()}
             out["cl1"] = cl1
-        q.put((rank, out))
+        q.put((rank, _np(out)))
     finally:
         dist.destroy_process_group()
 
@@ -155,5 +165,58 @@ def test_data_parallel_calibration_two_gpus():
     r0, r1 = res[0], res[1]
     assert r0["cl"] == r1["cl"] == r0["cl1"]
     for k, v in r0["sal1"].items():
-        assert torch.equal(r0["sal"][k], r1["sal"][k]), k
-        assert torch.allclose(r0["sal"][k], v, rtol=1e-3, atol=1e-12), k
+        a, b, one = torch.from_numpy(r0["sal"][k]), torch.from_numpy(r1["sal"][k]), torch.from_numpy(v)
+        assert torch.equal(a, b), k
+        assert torch.allclose(a, one, rtol=1e-3, atol=1e-12), k
+
+
+def _rowq_worker(rank, world, port, q):
+    import torch.distributed as dist
+    from datetime import timedelta
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    dev = torch.device("cuda", rank)
+    torch.cuda.set_device(dev)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=120), device_id=dev)
+    try:
+        from csaq.kernels import quantize_per_channel
+        W = (torch.randn(1000, 1024, generator=torch.Generator().manual_seed(8)) * 0.02).to(torch.bfloat16).to(dev)
+        W[torch.arange(0, 1000, 97)] *= 10.0
+        out = {}
+        n = W.shape[0] // world
+        for bits in (2, 4, 8):
+            for gs in (128, -1):
+                mine = quantize_per_channel(W[rank * n:(rank + 1) * n], bits, gs)
+                parts = {}
+                for name, t in (("q", mine.qdata), ("s", mine.scales), ("z", mine.zero_points)):
+                    t = t.contiguous().to(dev)
+                    gathered = [torch.empty_like(t) for _ in range(world)]
+                    dist.all_gather(gathered, t)
+                    parts[name] = torch.cat(gathered)
+                full = quantize_per_channel(W, bits, gs)
+                out[(bits, gs)] = all(torch.equal(parts[k], v.to(dev)) for k, v in
+                                      (("q", full.qdata), ("s", full.scales), ("z", full.zero_points)))
+        q.put((rank, out))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_row_parallel_quantisation_two_gpus():
+    """Rows quantise independently (csaq/kernels.py:77-158): two ranks
+    quantising their halves of the rows and all-gathering codes, scales and
+    zero points reproduce the one-GPU quantisation bit for bit, with no other
+    exchange."""
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    import torch.multiprocessing as mp
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_rowq_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = dict(q.get(timeout=600) for _ in range(2))
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    for r in (0, 1):
+        assert all(res[r].values()), res[r]
