@@ -654,6 +654,18 @@ extern "C" int64_t csaq_attention_workspace_floats(int64_t B, int64_t S, int64_t
   return B * Hkv * n_split * S * (Hq / Hkv) * (D + 2);
 }
 
+// multiprocessors of the current device (looked up once)
+int sm_count() {
+  static int n = 0;
+  if (n <= 0) {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess ||
+        cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0)
+      n = 148;
+  }
+  return n;
+}
+
 // dynamic shared memory of the staged query rows, at least kAttnSpreadBytes:
 // with the static K/V tiles that is more than half an SM's shared memory, so
 // the CTAs of a launch land on distinct SMs even when the launch starts while
@@ -670,7 +682,9 @@ static int launch_attention(int64_t D, dim3 grid, cudaStream_t st, const void* q
   auto kern = D == 64 ? attention_kernel<T, 64, ROPE> : attention_kernel<T, 128, ROPE>;
   int64_t qbytes = S * (Hq / Hkv) * D * (int64_t)sizeof(T);
   if (qbytes > kAttnQBytesMax) return CSAQ_ERR_UNSUPPORTED;
-  qbytes = qbytes > kAttnSpreadBytes ? qbytes : kAttnSpreadBytes;
+  // spread only a grid that fits one wave: a larger one (many sequences) keeps
+  // several CTAs per SM rather than running wave after wave
+  if ((int64_t)grid.x * grid.y <= sm_count()) qbytes = qbytes > kAttnSpreadBytes ? qbytes : kAttnSpreadBytes;
   static bool opted[2] = {false, false};
   bool& done = opted[D == 64 ? 0 : 1];
   if (!done) {
