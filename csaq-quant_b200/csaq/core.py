@@ -224,6 +224,7 @@ class CausalProfiler:
             self.salience[name] = torch.zeros(module.weight.shape, dtype=torch.float32, device=mdev)
             self._masks[name] = MaskHistory(module.weight.shape[0], mdev)
             self._register_hook(name, module)
+            self._register_salience_hook(name, module)
 
     def _register_hook(self, name: str, module: nn.Linear) -> None:
         alpha = self.config.salience_alpha
@@ -236,6 +237,31 @@ class CausalProfiler:
                 self._masks[name].append(out, mode=1, k=k)
 
         self._hooks.append(module.register_forward_hook(forward_hook))
+
+    def _register_salience_hook(self, name: str, module: nn.Linear) -> None:
+        """|grad * W| (csaq/core.py:204-210) accumulated as soon as the weight's
+        gradient is complete, during the backward pass, and the gradient freed
+        right away: the salience kernels overlap the rest of the backward and
+        the gradients of all layers never coexist (16 GB of bf16 gradients at
+        the Llama-3-8B shape). A batch whose backward fails part-way keeps
+        the salience of the layers whose gradients had completed (the
+        reference, which accumulates after the backward, drops the batch)."""
+        w = module.weight
+        if not hasattr(w, "register_post_accumulate_grad_hook"):
+            return
+
+        def hook(param: torch.Tensor) -> None:
+            if param.grad is None:
+                return
+            acc = self.salience[name]
+            g, data = param.grad, param.data
+            if not g.is_cuda:
+                g, data = g.to(acc.device), data.to(acc.device)
+            with torch.no_grad():
+                salience_accumulate(acc, g, data)
+            param.grad = None
+
+        self._hooks.append(w.register_post_accumulate_grad_hook(hook))
 
     def add_activation_masks(self, name: str, act: torch.Tensor, threshold: Optional[float] = None) -> None:
         """Append co-activation masks from activations directly: act > threshold
@@ -276,7 +302,7 @@ class CausalProfiler:
                 warnings.warn(f"[CSAQ] Skipping calibration batch {i}: {exc}")
                 self.model.zero_grad()
                 continue
-            with torch.no_grad():
+            with torch.no_grad():  # weights without the gradient hook (accumulated there otherwise)
                 for name, module in self._modules.items():
                     if module.weight.grad is not None:
                         acc = self.salience[name]
