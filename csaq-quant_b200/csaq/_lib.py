@@ -51,6 +51,15 @@ class CsaqTier(ctypes.Structure):
     ]
 
 
+class CsaqGemvExt(ctypes.Structure):
+    """Mirror of ``csaq_gemv_ext`` (include/csaq_b200.h)."""
+
+    _fields_ = [
+        ("silu_tiers", ctypes.c_uint32),
+        ("x_mul", c_vp),
+    ]
+
+
 MAX_RANKS = 8
 IPC_HANDLE_BYTES = 64
 
@@ -92,6 +101,8 @@ _SIGNATURES = {
     "csaq_qgemm_wait_timeouts": (c_int, [ctypes.POINTER(c_i64)]),
     "csaq_qgemv": (c_int, [ctypes.POINTER(CsaqTier), c_int, c_i64, c_vp, c_int, c_i64, c_i64, c_vp]),
     "csaq_qgemv_simt": (c_int, [ctypes.POINTER(CsaqTier), c_int, c_i64, c_vp, c_int, c_i64, c_i64, c_vp]),
+    "csaq_qgemv_ext": (c_int, [ctypes.POINTER(CsaqTier), c_int, c_i64, c_vp, c_int, c_i64, c_i64,
+                               ctypes.POINTER(CsaqGemvExt), c_vp]),
     "csaq_tile_blocks_bytes": (c_i64, [c_int, c_i64, c_i64]),
     "csaq_repack_tiles": (c_int, [ctypes.POINTER(CsaqTier), c_i64, c_vp, c_vp]),
     "csaq_act_mask": (c_int, [c_vp, c_int, c_i64, c_i64, c_i64, c_int, ctypes.c_float, c_i64, c_vp, c_vp,

@@ -90,6 +90,8 @@ class _Shape:
     logits: torch.Tensor
     part: torch.Tensor
     descs: Dict  # (layer, name, verify) -> ctypes array + count
+    gate_mask: Dict = None  # (layer, verify) -> bit mask of the gate tiers of the fused gate/up launch
+    fuse_gate: bool = False  # the SiLU gate runs inside the gate/up and down GEMVs (csaq_qgemv_ext)
     y_part: Optional[torch.Tensor] = None    # TP: this rank's partial o/down output (M, H)
     y_all: Optional[torch.Tensor] = None     # TP: all ranks' partials (W, M, H)
     logits_all: Optional[torch.Tensor] = None  # TP: all ranks' vocabulary slices (W, M, V/W)
@@ -308,7 +310,11 @@ class DecodeRuntime:
         sh = _Shape(S=S, M=M, x=mk(M, H), xn=mk(M, H), qkv=mk(M, nq + 2 * nkv), q_rot=mk(M, nq),
                     attn=mk(M, nq), gu=mk(M, 2 * I), h=mk(M, I), logits=mk(M, self.Vl),
                     part=torch.zeros(max(part_n, 1), dtype=torch.float32, device=self.dev),
-                    descs={})
+                    descs={}, gate_mask={})
+        # the SiLU gate fused into the gate/up and down GEMVs when both run the
+        # tensor-core kernel (CSAQ_FUSE_GATE=0 keeps the separate csaq_silu_mul)
+        fuse = (os.environ.get("CSAQ_FUSE_GATE", "1") != "0" and H % 128 == 0 and I % 128 == 0
+                and self.dtype in (torch.bfloat16, torch.float16))
         if W > 1:
             sh.y_part, sh.y_all, sh.logits_all = mk(M, H), mk(W, M, H), mk(W, M, self.Vl)
         # at TP 1 the o/down GEMVs add the residual in their epilogue; with
@@ -330,6 +336,10 @@ class DecodeRuntime:
                             d.y, d.ldy = self.p2p.part_ptr(parity), H
                 for name, d in (("qkv", qkv), ("o", o), ("gu", gu), ("down", dn)):
                     sh.descs[(li, name, verify)] = (_lib.tier_array(d), len(d))
+                n_gate = len(mods["gate"].gemv_descriptors(sh.gu[:, :I], verify))
+                sh.gate_mask[(li, verify)] = (1 << n_gate) - 1
+                fuse = fuse and all(t.blocks or t.n_rows == 0 for t in gu + dn)
+        sh.fuse_gate = fuse
         d = self.lm_head.gemv_descriptors(sh.logits)
         sh.descs[("lm", "all")] = (_lib.tier_array(d), len(d))
         d = self.lm_head.gemv_descriptors(sh.logits[: self.B])
@@ -346,6 +356,19 @@ class DecodeRuntime:
             check(lib().csaq_qgemm(arr, n, K, x.data_ptr(), self.dt, M, x.stride(0), st), "qgemm")
         else:
             check(lib().csaq_qgemv(arr, n, K, x.data_ptr(), self.dt, M, x.stride(0), st), "qgemv")
+
+    @staticmethod
+    def _fused_gate(sh: "_Shape") -> bool:
+        return sh.fuse_gate and sh.M < RUNTIME_GEMM_MIN_TOKENS
+
+    def _gemv_ext(self, arr_n, K: int, x: torch.Tensor, M: int, st: int, silu_tiers: int = 0,
+                  x_mul: Optional[torch.Tensor] = None) -> None:
+        """The GEMV with the SiLU gate fused in: silu_tiers stores silu(y) for
+        the gate tiers; x_mul makes the input dtype(x * x_mul) (g' * u)."""
+        arr, n = arr_n
+        ext = _lib.CsaqGemvExt(silu_tiers, x_mul.data_ptr() if x_mul is not None else None)
+        check(lib().csaq_qgemv_ext(arr, n, K, x.data_ptr(), self.dt, M, x.stride(0), ctypes.byref(ext), st),
+              "qgemv_ext")
 
     def _p2p_for(self, M: int) -> bool:
         return self.p2p is not None and M <= self.p2p.rows
@@ -415,6 +438,7 @@ class DecodeRuntime:
         nq, nkv = Hq * D, Hkv * D
         torch.index_select(self.embed, 0, ids.view(-1), out=sh.x)
         scale = 1.0 / math.sqrt(D)
+        fgate = self._fused_gate(sh)
         for li, layer in enumerate(self.layers):
             check(L.csaq_rmsnorm(sh.x.data_ptr(), H, layer.input_layernorm.weight.data_ptr(),
                                  sh.xn.data_ptr(), H, M, H, self.eps, self.dt, st), "rmsnorm")
@@ -425,10 +449,14 @@ class DecodeRuntime:
                 self._combine(sh, M, st, 0)
             check(L.csaq_rmsnorm(sh.x.data_ptr(), H, layer.post_attention_layernorm.weight.data_ptr(),
                                  sh.xn.data_ptr(), H, M, H, self.eps, self.dt, st), "rmsnorm")
-            self._gemv(sh.descs[(li, "gu", verify)], H, sh.xn, M, st)
-            check(L.csaq_silu_mul(sh.gu.data_ptr(), sh.gu.stride(0), sh.gu[:, I:].data_ptr(),
-                                  sh.gu.stride(0), sh.h.data_ptr(), I, M, I, self.dt, st), "silu_mul")
-            self._gemv(sh.descs[(li, "down", verify)], I, sh.h, M, st)
+            if fgate:  # gate tiers store silu(y); the down GEMV multiplies g' and u in its record build
+                self._gemv_ext(sh.descs[(li, "gu", verify)], H, sh.xn, M, st, silu_tiers=sh.gate_mask[(li, verify)])
+                self._gemv_ext(sh.descs[(li, "down", verify)], I, sh.gu, M, st, x_mul=sh.gu[:, I:])
+            else:
+                self._gemv(sh.descs[(li, "gu", verify)], H, sh.xn, M, st)
+                check(L.csaq_silu_mul(sh.gu.data_ptr(), sh.gu.stride(0), sh.gu[:, I:].data_ptr(),
+                                      sh.gu.stride(0), sh.h.data_ptr(), I, M, I, self.dt, st), "silu_mul")
+                self._gemv(sh.descs[(li, "down", verify)], I, sh.h, M, st)
             if self.tp > 1:
                 self._combine(sh, M, st, 1)
         check(L.csaq_rmsnorm(sh.x.data_ptr(), H, self.final_norm.data_ptr(), sh.xn.data_ptr(), H, M, H,
@@ -473,13 +501,14 @@ class DecodeRuntime:
     def kernels_per_step(self, S: int) -> int:
         """Own (libcsaq) kernel launches in one step of up to 16 tokens per
         GEMV launch: per layer 2 RMSNorm, 4 GEMV, RoPE with attention (one
-        launch), SiLU (and 2 rank-order combines under TP); plus the final
-        RMSNorm, the lm_head GEMV and the argmax."""
-        return self.n_layers * (8 + (2 if self.tp > 1 else 0)) + 3
+        launch), SiLU unless the GEMVs run it (and 2 rank-order combines under
+        TP); plus the final RMSNorm, the lm_head GEMV and the argmax."""
+        silu = 0 if self._fused_gate(self._shape(S)) else 1
+        return self.n_layers * (7 + silu + (2 if self.tp > 1 else 0)) + 3
 
     def prefill_kernels(self, P: int, verify: bool = True) -> int:
         """Own kernel launches of reset() for a P-token prompt: per chunk and
-        layer 2 RMSNorm, RoPE, SiLU, the decode attention kernel for chunks
+        layer 2 RMSNorm, RoPE, SiLU (unless inside the GEMVs), the decode attention kernel for chunks
         below PREFILL_SDPA_TOKENS (torch's fused attention above), the
         combines under TP, and the linears (one tcgen05 GEMM launch per tier
         from RUNTIME_GEMM_MIN_TOKENS tokens, else one GEMV launch per 16 tokens
@@ -496,7 +525,8 @@ class DecodeRuntime:
                         n += sum(1 for i in range(nd) if arr[i].n_rows > 0)
                     else:
                         n += -(-M // 16)
-                n += 4 + (2 if self.tp > 1 else 0)  # 2 RMSNorm, SiLU, RoPE (+ SDPA) or fused RoPE + attention
+                silu = 0 if self._fused_gate(sh) else 1  # SiLU, unless inside the GEMVs
+                n += 3 + silu + (2 if self.tp > 1 else 0)  # 2 RMSNorm, RoPE (+ SDPA) or fused RoPE + attention
             n += 2
         return n + 1
 

@@ -312,6 +312,8 @@ struct KParams {
   int x_bytes;     // R4 records: n_rec * M * kRecStride (R2 the same again when want2)
   int split;       // records split by chunk between the cluster's CTAs (they do not fit one)
   int ch_half;     // split: CTA rank 0 holds chunks [0, ch_half), rank 1 the rest
+  uint32_t silu_tiers;  // bit i: tier i stores dtype(silu(y))
+  const void* x_mul;   // nullable: the input is dtype(x * x_mul), rows ldx apart
   int begin[kMaxWarps + 1];
 };
 
@@ -352,8 +354,20 @@ struct OutDesc {
 
 CSAQ_GUARD_RECORD()
 
+// The stored value: dtype(v), or for a gate tier the SiLU of it as the
+// separate gate kernel computes it, g = float(dtype(v)), dtype(g / (1 +
+// exp(-g))) (silu_mul_kernel, runtime.cu).
+template <typename ACT>
+__device__ __forceinline__ ACT out_value(float v, bool silu) {
+  if (silu) {
+    const float g = to_f32<ACT>(from_f32<ACT>(v));
+    v = g / (1.0f + __expf(-g));
+  }
+  return from_f32<ACT>(v);
+}
+
 template <typename ACT, typename TD>
-__device__ __forceinline__ void store_out(const TD& T, int row, int tok, float v, float xe) {
+__device__ __forceinline__ void store_out(const TD& T, int row, int tok, float v, float xe, bool silu) {
   v = __fmul_rn(v, xe);
   const int orow = T.out_rows[row];
   if (!CSAQ_GUARD(orow >= 0 && orow < T.ldy && (!T.residual || orow < T.ldr), CSAQ_GUARD_GEMV_OUT_ROW, orow,
@@ -362,7 +376,7 @@ __device__ __forceinline__ void store_out(const TD& T, int row, int tok, float v
   if (T.bias) v = __fadd_rn(v, to_f32<ACT>(reinterpret_cast<const ACT*>(T.bias)[orow]));
   if (T.residual)
     v = __fadd_rn(v, to_f32<ACT>(reinterpret_cast<const ACT*>(T.residual)[(int64_t)tok * T.ldr + orow]));
-  reinterpret_cast<ACT*>(T.y)[(int64_t)tok * T.ldy + orow] = from_f32<ACT>(v);
+  reinterpret_cast<ACT*>(T.y)[(int64_t)tok * T.ldy + orow] = out_value<ACT>(v, silu);
 }
 
 // ── bulk copies into the per-warp ring (one elected lane; no multicast) ────
@@ -653,6 +667,7 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kThreads, 1)
   const int c_lo = SPLIT ? rank * P.ch_half : 0;
   const int n_loc = SPLIT ? (rank == 0 ? P.ch_half : n_chunks - P.ch_half) : n_chunks;
   const int n_st = M * n_loc * 4;
+  const bool gated = P.x_mul != nullptr;
   for (int base = 0; base < n_st; base += blockDim.x) {
     const int u = base + threadIdx.x;
     const bool live = u < n_st;
@@ -664,11 +679,26 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kThreads, 1)
     // [2^14, 2^15), exact for bf16/fp16) from the 4 lanes of the (chunk, token)
     float xv[32];
     float mx = 0.0f;
+    const int64_t xo = (int64_t)tok * ldx + ch * 128 + cc * 32;
+    uint4 q[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) q[i] = live ? ld_cached_v4(x + xo + 8 * i) : make_uint4(0u, 0u, 0u, 0u);
+    if (gated) {  // h = dtype(g' * u), as silu_mul_kernel stores it
+      const ACT* xm = reinterpret_cast<const ACT*>(P.x_mul);
+      uint4 q2[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) q2[i] = live ? ld_cached_v4(xm + xo + 8 * i) : make_uint4(0u, 0u, 0u, 0u);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        ACT* e = reinterpret_cast<ACT*>(&q[i]);
+        const ACT* e2 = reinterpret_cast<const ACT*>(&q2[i]);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) e[j] = from_f32<ACT>(to_f32<ACT>(e[j]) * to_f32<ACT>(e2[j]));
+      }
+    }
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
-      const uint4 q = live ? ld_cached_v4(x + (int64_t)tok * ldx + ch * 128 + cc * 32 + 8 * i)
-                           : make_uint4(0u, 0u, 0u, 0u);
-      const ACT* e = reinterpret_cast<const ACT*>(&q);
+      const ACT* e = reinterpret_cast<const ACT*>(&q[i]);
 #pragma unroll
       for (int j = 0; j < 8; ++j) {
         xv[8 * i + j] = to_f32<ACT>(e[j]);
@@ -774,7 +804,7 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kThreads, 1)
 #pragma unroll
           for (int e = 0; e < 4; ++e) {
             const int row = unit * c_mt * kTileRows + frag_row(mt, e, lane), tok = frag_tok(nt, e, lane);
-            if (mt < c_mt && tok < M && row < T.n_rows) store_out<ACT>(T, row, tok, acc[mt][nt][e], xexp[tok]);
+            if (mt < c_mt && tok < M && row < T.n_rows) store_out<ACT>(T, row, tok, acc[mt][nt][e], xexp[tok], (P.silu_tiers >> t) & 1u);
           }
     } else if (item == it_begin) {
       cut_t0 = t; cut_u0 = unit; cut_s0 = u_start;
@@ -804,6 +834,7 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kThreads, 1)
   const int b_lane = pin(P.begin[cl_base + lane]), b_end = pin(P.begin[cl_base + 32]);
   const int t_own = cut_t0 >= 0 ? cut_t0 : 0;
   const int own_rows = pin(P.w[t_own].mt) * kTileRows;
+  const bool own_silu = (P.silu_tiers >> t_own) & 1u;
   OutDesc od;
   od.out_rows = pin(P.tp.t[t_own].out_rows);
   od.bias = pin(P.tp.t[t_own].bias);
@@ -904,7 +935,7 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kThreads, 1)
     for (int j = 0; j < 16; ++j) {
       if (j >= nv) break;
       const int e = lane + 32 * j, r = e / M, tok = e - r * M, row = unit * rows + r;
-      if (e < n_val && row < od.n_rows) store_out<ACT>(od, row, tok, v[j], xexp[tok]);
+      if (e < n_val && row < od.n_rows) store_out<ACT>(od, row, tok, v[j], xexp[tok], own_silu);
     }
   }
   cluster_wait();  // no CTA leaves while the other may still read its partials
@@ -1193,7 +1224,8 @@ int set_smem_attr() {
 }
 
 template <typename ACT, int NT>
-int launch_mma_block(const TierParams& TP, int64_t K, const ACT* x, int M, int64_t ldx, cudaStream_t st) {
+int launch_mma_block(const TierParams& TP, int64_t K, const ACT* x, int M, int64_t ldx, const csaq_gemv_ext& ext,
+                     const ACT* x_mul, cudaStream_t st) {
   Plan pl;
   if (!make_plan(TP, K, M, pl)) return CSAQ_ERR_UNSUPPORTED;
   int rc = pl.split ? set_smem_attr<ACT, NT, true>() : set_smem_attr<ACT, NT, false>();
@@ -1210,6 +1242,8 @@ int launch_mma_block(const TierParams& TP, int64_t K, const ACT* x, int M, int64
   P.x_bytes = pl.x_bytes;
   P.split = pl.split;
   P.ch_half = pl.ch_half;
+  P.silu_tiers = ext.silu_tiers;
+  P.x_mul = x_mul;
   // the grid depends on the shapes and the SM count only (never on M)
   int ctas = (items + kWarps - 1) / kWarps;
   ctas = (ctas + kCluster - 1) / kCluster * kCluster;
@@ -1224,7 +1258,9 @@ int launch_mma_block(const TierParams& TP, int64_t K, const ACT* x, int M, int64
 }
 
 template <typename ACT>
-int launch_mma(const TierParams& P0, int64_t K, const void* x, int64_t M, int64_t ldx, cudaStream_t st) {
+int launch_mma(const TierParams& P0, int64_t K, const void* x, int64_t M, int64_t ldx, cudaStream_t st,
+               const csaq_gemv_ext* ext_in = nullptr) {
+  const csaq_gemv_ext ext = ext_in ? *ext_in : csaq_gemv_ext{0u, nullptr};
   if (P0.tile_start[P0.n_tiers] == 0) return CSAQ_OK;
   int64_t m0 = 0;
   while (m0 < M) {
@@ -1238,8 +1274,9 @@ int launch_mma(const TierParams& P0, int64_t K, const void* x, int64_t M, int64_
         P.t[i].residual = reinterpret_cast<const ACT*>(P.t[i].residual) + m0 * P.t[i].ldr;
     }
     const ACT* xb = reinterpret_cast<const ACT*>(x) + m0 * ldx;
-    const int rc = mb <= 8 ? launch_mma_block<ACT, 1>(P, K, xb, mb, ldx, st)
-                           : launch_mma_block<ACT, 2>(P, K, xb, mb, ldx, st);
+    const ACT* xm = ext.x_mul ? reinterpret_cast<const ACT*>(ext.x_mul) + m0 * ldx : nullptr;
+    const int rc = mb <= 8 ? launch_mma_block<ACT, 1>(P, K, xb, mb, ldx, ext, xm, st)
+                           : launch_mma_block<ACT, 2>(P, K, xb, mb, ldx, ext, xm, st);
     if (rc) return rc;
     m0 += mb;
   }
@@ -1313,6 +1350,21 @@ extern "C" int csaq_qgemv(const csaq_tier* tiers, int n_tiers, int64_t K, const 
   if (x_dtype == CSAQ_DT_F32) return launch_simt<float>(P, K, x, M, ldx, st);
   return x_dtype == CSAQ_DT_BF16 ? launch_simt<__nv_bfloat16>(P, K, x, M, ldx, st)
                                  : launch_simt<__half>(P, K, x, M, ldx, st);
+}
+
+extern "C" int csaq_qgemv_ext(const csaq_tier* tiers, int n_tiers, int64_t K, const void* x, int x_dtype,
+                              int64_t M, int64_t ldx, const csaq_gemv_ext* ext, void* stream) {
+  TierParams P;
+  int rc = build_params(tiers, n_tiers, K, P);
+  if (rc) return rc;
+  if (!x || !ext || M < 0 || ldx < K || !dtype_size(x_dtype)) return CSAQ_ERR_ARG;
+  if ((ext->silu_tiers >> n_tiers) != 0u) return CSAQ_ERR_ARG;  // n_tiers <= CSAQ_MAX_TIERS (build_params)
+  if (x_dtype == CSAQ_DT_F32 || !mma_eligible(P, K, x, ldx)) return CSAQ_ERR_UNSUPPORTED;
+  if (ext->x_mul && reinterpret_cast<uintptr_t>(ext->x_mul) % 16) return CSAQ_ERR_UNSUPPORTED;
+  if (M == 0) return CSAQ_OK;
+  cudaStream_t st = as_stream(stream);
+  return x_dtype == CSAQ_DT_BF16 ? launch_mma<__nv_bfloat16>(P, K, x, M, ldx, st, ext)
+                                 : launch_mma<__half>(P, K, x, M, ldx, st, ext);
 }
 
 extern "C" int csaq_qgemv_simt(const csaq_tier* tiers, int n_tiers, int64_t K, const void* x,

@@ -165,6 +165,21 @@ int csaq_repack_tiles(const csaq_tier* tier, int64_t K, uint8_t* blocks, void* s
 int csaq_qgemv(const csaq_tier* tiers, int n_tiers, int64_t K, const void* x, int x_dtype,
                int64_t M, int64_t ldx, void* stream);
 
+/* The HF LlamaMLP gate fused into the tensor-core GEMV, for the decode
+ * runtime (no reference counterpart; the reference runs act_fn(gate(x)) *
+ * up(x) as separate torch ops). Bit i of silu_tiers: tier i stores
+ * dtype(silu(y)), y the value csaq_qgemv would store (the gate tiers of a
+ * fused gate/up launch). x_mul non-null: the input is h = dtype(x * x_mul),
+ * elementwise, x_mul M x ldx like x (the down projection reading g' and u).
+ * Together they give bit for bit csaq_qgemv, csaq_silu_mul, csaq_qgemv.
+ * Needs the tensor-core kernel's conditions (else CSAQ_ERR_UNSUPPORTED). */
+typedef struct csaq_gemv_ext {
+  uint32_t silu_tiers;
+  const void* x_mul;
+} csaq_gemv_ext;
+int csaq_qgemv_ext(const csaq_tier* tiers, int n_tiers, int64_t K, const void* x, int x_dtype,
+                   int64_t M, int64_t ldx, const csaq_gemv_ext* ext, void* stream);
+
 /* The same product for many tokens (prefill / verify with M in the tens to
  * thousands), on the tcgen05 tensor cores: X (bf16 or fp16) times the tier
  * weights dequantised in shared memory to X's dtype, exactly as the
