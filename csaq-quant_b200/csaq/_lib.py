@@ -136,6 +136,8 @@ _SIGNATURES = {
     "csaq_ipc_close": (c_int, [c_vp]),
     "csaq_tp_exchange_sum": (c_int, [ctypes.POINTER(CsaqP2PGroup), c_i64, c_i64, c_vp, c_i64, c_i64, c_i64, c_int,
                                      c_vp]),
+    "csaq_tp_exchange_sum_rmsnorm": (c_int, [ctypes.POINTER(CsaqP2PGroup), c_i64, c_i64, c_vp, c_i64, c_i64, c_i64,
+                                             c_vp, c_vp, c_i64, ctypes.c_float, c_int, c_vp]),
     "csaq_p2p_errors": (c_int, [ctypes.POINTER(CsaqP2PGroup), ctypes.POINTER(c_i64)]),
     "csaq_p2p_set_spin_limit": (c_int, [c_i64]),
     "csaq_silu_mul": (c_int, [c_vp, c_i64, c_vp, c_i64, c_vp, c_i64, c_i64, c_i64, c_int, c_vp]),

@@ -272,6 +272,9 @@ class DecodeRuntime:
             self.p2p = _P2PExchange(tp_group, self.tp_rank, W, rows, self.H, self.embed.element_size(), self.dev)
         self.graphs: Dict[str, torch.cuda.CUDAGraph] = {}
         self.launches_per_step: Dict[str, int] = {}
+        # the peer-memory combines also run the RMSNorm that follows them
+        # (CSAQ_TP_FUSE_NORM=0 keeps a separate csaq_rmsnorm launch)
+        self.fuse_tp_norm = os.environ.get("CSAQ_TP_FUSE_NORM", "1") != "0"
 
     def release(self) -> None:
         """Drop the captured graphs and, under TP, the peer-memory buffers
@@ -373,19 +376,28 @@ class DecodeRuntime:
     def _p2p_for(self, M: int) -> bool:
         return self.p2p is not None and M <= self.p2p.rows
 
-    def _combine(self, sh: _Shape, M: int, st: int, parity: int) -> None:
+    def _combine(self, sh: _Shape, M: int, st: int, parity: int, norm_w: Optional[torch.Tensor] = None) -> bool:
         """TP: add every rank's partial o (parity 0) or down (parity 1) output
         to x in rank order: through peer memory when the step fits the
-        exchange buffers, else an NCCL all-gather and csaq_rank_sum."""
+        exchange buffers, else an NCCL all-gather and csaq_rank_sum. Through
+        peer memory with norm_w given, the same launch also writes
+        xn = RMSNorm(x) with those weights; returns whether it did."""
+        if self._p2p_for(M) and norm_w is not None and self.fuse_tp_norm:
+            check(lib().csaq_tp_exchange_sum_rmsnorm(ctypes.byref(self.p2p.group), parity * self.p2p.rows * self.H,
+                                                     self.H, sh.x.data_ptr(), self.H, M, self.H, norm_w.data_ptr(),
+                                                     sh.xn.data_ptr(), self.H, self.eps, self.dt, st),
+                  "tp_exchange_rmsnorm")
+            return True
         if self._p2p_for(M):
             check(lib().csaq_tp_exchange_sum(ctypes.byref(self.p2p.group), parity * self.p2p.rows * self.H, self.H,
                                              sh.x.data_ptr(), self.H, M, self.H, self.dt, st), "tp_exchange")
-            return
+            return False
         import torch.distributed as dist
         dist.all_gather_into_tensor(sh.y_all[:, :M], sh.y_part[:M], group=self.tp_group)
         H = self.H
         check(lib().csaq_rank_sum(sh.y_all.data_ptr(), self.tp, sh.y_all.stride(0), H, sh.x.data_ptr(), H, M, H, 1,
                                   self.dt, st), "rank_sum")
+        return False
 
     def _attention(self, li: int, sh: "_Shape", S: int, pos: torch.Tensor, pos_host: Optional[int],
                    scale: float, st: int) -> None:
@@ -439,16 +451,19 @@ class DecodeRuntime:
         torch.index_select(self.embed, 0, ids.view(-1), out=sh.x)
         scale = 1.0 / math.sqrt(D)
         fgate = self._fused_gate(sh)
+        n_layers = len(self.layers)
+        xn_ready = False  # the previous combine already wrote this layer's input norm into xn
         for li, layer in enumerate(self.layers):
-            check(L.csaq_rmsnorm(sh.x.data_ptr(), H, layer.input_layernorm.weight.data_ptr(),
-                                 sh.xn.data_ptr(), H, M, H, self.eps, self.dt, st), "rmsnorm")
+            if not xn_ready:
+                check(L.csaq_rmsnorm(sh.x.data_ptr(), H, layer.input_layernorm.weight.data_ptr(),
+                                     sh.xn.data_ptr(), H, M, H, self.eps, self.dt, st), "rmsnorm")
             self._gemv(sh.descs[(li, "qkv", verify)], H, sh.xn, M, st)
             self._attention(li, sh, S, pos, pos_host, scale, st)
             self._gemv(sh.descs[(li, "o", verify)], nq, sh.attn, M, st)
-            if self.tp > 1:
-                self._combine(sh, M, st, 0)
-            check(L.csaq_rmsnorm(sh.x.data_ptr(), H, layer.post_attention_layernorm.weight.data_ptr(),
-                                 sh.xn.data_ptr(), H, M, H, self.eps, self.dt, st), "rmsnorm")
+            post = layer.post_attention_layernorm.weight
+            if not (self.tp > 1 and self._combine(sh, M, st, 0, norm_w=post)):
+                check(L.csaq_rmsnorm(sh.x.data_ptr(), H, post.data_ptr(),
+                                     sh.xn.data_ptr(), H, M, H, self.eps, self.dt, st), "rmsnorm")
             if fgate:  # gate tiers store silu(y); the down GEMV multiplies g' and u in its record build
                 self._gemv_ext(sh.descs[(li, "gu", verify)], H, sh.xn, M, st, silu_tiers=sh.gate_mask[(li, verify)])
                 self._gemv_ext(sh.descs[(li, "down", verify)], I, sh.gu, M, st, x_mul=sh.gu[:, I:])
@@ -457,10 +472,11 @@ class DecodeRuntime:
                 check(L.csaq_silu_mul(sh.gu.data_ptr(), sh.gu.stride(0), sh.gu[:, I:].data_ptr(),
                                       sh.gu.stride(0), sh.h.data_ptr(), I, M, I, self.dt, st), "silu_mul")
                 self._gemv(sh.descs[(li, "down", verify)], I, sh.h, M, st)
-            if self.tp > 1:
-                self._combine(sh, M, st, 1)
-        check(L.csaq_rmsnorm(sh.x.data_ptr(), H, self.final_norm.data_ptr(), sh.xn.data_ptr(), H, M, H,
-                             self.eps, self.dt, st), "rmsnorm")
+            nxt = self.layers[li + 1].input_layernorm.weight if li + 1 < n_layers else self.final_norm
+            xn_ready = self.tp > 1 and self._combine(sh, M, st, 1, norm_w=nxt)
+        if not xn_ready:
+            check(L.csaq_rmsnorm(sh.x.data_ptr(), H, self.final_norm.data_ptr(), sh.xn.data_ptr(), H, M, H,
+                                 self.eps, self.dt, st), "rmsnorm")
         if last_only and S > 1:
             arr, n = sh.descs[("lm", "last")]
             last = sh.xn[S - 1:]  # rows S-1, 2S-1, ...: the last token of each sequence
@@ -502,9 +518,18 @@ class DecodeRuntime:
         """Own (libcsaq) kernel launches in one step of up to 16 tokens per
         GEMV launch: per layer 2 RMSNorm, 4 GEMV, RoPE with attention (one
         launch), SiLU unless the GEMVs run it (and 2 rank-order combines under
-        TP); plus the final RMSNorm, the lm_head GEMV and the argmax."""
-        silu = 0 if self._fused_gate(self._shape(S)) else 1
-        return self.n_layers * (7 + silu + (2 if self.tp > 1 else 0)) + 3
+        TP, which through peer memory also run the RMSNorm that follows
+        them); plus the final RMSNorm, the lm_head GEMV and the argmax."""
+        sh = self._shape(S)
+        silu = 0 if self._fused_gate(sh) else 1
+        norms = self._norm_launches(sh.M)
+        return self.n_layers * (5 + silu + (2 if self.tp > 1 else 0)) + norms + 2
+
+    def _norm_launches(self, M: int) -> int:
+        """Separate RMSNorm launches of one step of M tokens: 2 per layer and
+        the final one, or only the first layer's input norm when the peer
+        memory combines run the others."""
+        return 1 if (self.tp > 1 and self._p2p_for(M) and self.fuse_tp_norm) else 2 * self.n_layers + 1
 
     def prefill_kernels(self, P: int, verify: bool = True) -> int:
         """Own kernel launches of reset() for a P-token prompt: per chunk and
@@ -526,8 +551,8 @@ class DecodeRuntime:
                     else:
                         n += -(-M // 16)
                 silu = 0 if self._fused_gate(sh) else 1  # SiLU, unless inside the GEMVs
-                n += 3 + silu + (2 if self.tp > 1 else 0)  # 2 RMSNorm, RoPE (+ SDPA) or fused RoPE + attention
-            n += 2
+                n += 1 + silu + (2 if self.tp > 1 else 0)  # RoPE (+ SDPA) or fused RoPE + attention
+            n += self._norm_launches(M) + 1  # the RMSNorms and the lm_head
         return n + 1
 
     # ── generation ──────────────────────────────────────────────────────────

@@ -23,6 +23,7 @@
 #include <atomic>
 
 #include "common.cuh"
+#include "rmsnorm.cuh"
 
 namespace csaq {
 namespace {
@@ -39,11 +40,9 @@ __device__ __forceinline__ uint64_t ld_acquire_sys(const uint64_t* p) {
   return v;
 }
 
-template <typename T>
-__global__ void tp_exchange_kernel(const csaq_p2p_group G, int64_t part_offset, int64_t ld_p, T* __restrict__ out,
-                                   int64_t ldo, int64_t M, int N, long long spin_limit) {
-  pdl_wait();  // this rank's partial, written by the previous kernel, is complete
-  pdl_trigger();
+// Steps 1 and 2 of the exchange (signal every peer, wait for every peer);
+// returns the new exchange count.
+__device__ __forceinline__ uint64_t exchange_signal_wait(const csaq_p2p_group& G, long long spin_limit) {
   __shared__ uint64_t s_seq;
   if (threadIdx.x == 0) s_seq = *G.seq;
   __syncthreads();
@@ -66,14 +65,11 @@ __global__ void tp_exchange_kernel(const csaq_p2p_group G, int64_t part_offset, 
     }
   }
   __syncthreads();
-  for (int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; i < M * N; i += int64_t(gridDim.x) * blockDim.x) {
-    const int64_t m = i / N, n = i - m * N;
-    float v = to_f32<T>(out[m * ldo + n]);
-    for (int r = 0; r < G.n_ranks; ++r)
-      v = __fadd_rn(v, to_f32<T>(__ldcg(reinterpret_cast<const T*>(G.parts[r]) + part_offset + m * ld_p + n)));  // not from L1
-    out[m * ldo + n] = from_f32<T>(v);
-  }
-  // the last CTA to finish advances the exchange count for the next launch
+  return want;
+}
+
+// the last CTA to finish advances the exchange count for the next launch
+__device__ __forceinline__ void exchange_done(const csaq_p2p_group& G, uint64_t want) {
   __syncthreads();
   if (threadIdx.x == 0) {
     __threadfence();
@@ -83,6 +79,124 @@ __global__ void tp_exchange_kernel(const csaq_p2p_group G, int64_t part_offset, 
       __threadfence();
     }
   }
+}
+
+template <typename T>
+__global__ void tp_exchange_kernel(const csaq_p2p_group G, int64_t part_offset, int64_t ld_p, T* __restrict__ out,
+                                   int64_t ldo, int64_t M, int N, long long spin_limit) {
+  pdl_wait();  // this rank's partial, written by the previous kernel, is complete
+  pdl_trigger();
+  const uint64_t want = exchange_signal_wait(G, spin_limit);
+  for (int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; i < M * N; i += int64_t(gridDim.x) * blockDim.x) {
+    const int64_t m = i / N, n = i - m * N;
+    float v = to_f32<T>(out[m * ldo + n]);
+    for (int r = 0; r < G.n_ranks; ++r)
+      v = __fadd_rn(v, to_f32<T>(__ldcg(reinterpret_cast<const T*>(G.parts[r]) + part_offset + m * ld_p + n)));  // not from L1
+    out[m * ldo + n] = from_f32<T>(v);
+  }
+  exchange_done(G, want);
+}
+
+// The exchange followed by the RMSNorm that reads its result (the next
+// layer's input norm or the post-attention norm), one CTA per row: the row's
+// sum out = T(out + sum_r part_r) in rank order exactly as tp_exchange_kernel
+// forms it, then xn = RMSNorm(out) exactly as rmsnorm_kernel does. One
+// launch instead of two, the same bits.
+template <typename T>
+__global__ void __launch_bounds__(kNormThreads)
+    tp_exchange_norm_kernel(const csaq_p2p_group G, int64_t part_offset, int64_t ld_p, T* __restrict__ out,
+                            int64_t ldo, int64_t M, int N, const T* __restrict__ w, T* __restrict__ xn,
+                            int64_t ldn, float eps, long long spin_limit) {
+  pdl_wait();
+  pdl_trigger();
+  const uint64_t want = exchange_signal_wait(G, spin_limit);
+  __shared__ float red[32];
+  const bool vec = N % 8 == 0 && N <= kNormThreads * 8 * kNormVec && ldo % 8 == 0 && ldn % 8 == 0 &&
+                   ld_p % 8 == 0 && part_offset % 8 == 0 && reinterpret_cast<uintptr_t>(out) % 16 == 0 &&
+                   reinterpret_cast<uintptr_t>(xn) % 16 == 0 && reinterpret_cast<uintptr_t>(w) % 16 == 0;
+  for (int64_t m = blockIdx.x; m < M; m += gridDim.x) {
+    T* orow = out + m * ldo;
+    if (vec) {
+      // the row's 16-byte vectors i = thread + j * kNormThreads, as rmsnorm_row
+      // assigns them: every rank's vectors are loaded before any is added, so
+      // the peers' partials cost one NVLink round trip
+      const int nv = N / 8;
+      uint4 xv[kNormVec], wv[kNormVec];
+      float acc[kNormVec][8];
+#pragma unroll
+      for (int j = 0; j < kNormVec; ++j) {
+        const int i = threadIdx.x + j * kNormThreads;
+        if (i < nv) {
+          xv[j] = reinterpret_cast<const uint4*>(orow)[i];
+          wv[j] = reinterpret_cast<const uint4*>(w)[i];
+        }
+      }
+#pragma unroll
+      for (int j = 0; j < kNormVec; ++j) {
+        const T* e = reinterpret_cast<const T*>(&xv[j]);
+#pragma unroll
+        for (int t = 0; t < 8; ++t) acc[j][t] = to_f32<T>(e[t]);
+      }
+      for (int r = 0; r < G.n_ranks; ++r) {
+        const uint4* pr = reinterpret_cast<const uint4*>(reinterpret_cast<const T*>(G.parts[r]) + part_offset + m * ld_p);
+        uint4 pv[kNormVec];
+#pragma unroll
+        for (int j = 0; j < kNormVec; ++j) {
+          const int i = threadIdx.x + j * kNormThreads;
+          if (i < nv) pv[j] = __ldcg(pr + i);  // not from L1
+        }
+#pragma unroll
+        for (int j = 0; j < kNormVec; ++j) {
+          const T* e = reinterpret_cast<const T*>(&pv[j]);
+#pragma unroll
+          for (int t = 0; t < 8; ++t) acc[j][t] = __fadd_rn(acc[j][t], to_f32<T>(e[t]));
+        }
+      }
+      // out = T(sum), then RMSNorm of the rounded row, as rmsnorm_row computes it
+      float ss = 0.0f;
+#pragma unroll
+      for (int j = 0; j < kNormVec; ++j) {
+        const int i = threadIdx.x + j * kNormThreads;
+        if (i < nv) {
+          T* e = reinterpret_cast<T*>(&xv[j]);
+#pragma unroll
+          for (int t = 0; t < 8; ++t) {
+            e[t] = from_f32<T>(acc[j][t]);
+            const float v = to_f32<T>(e[t]);
+            ss = fmaf(v, v, ss);
+          }
+          reinterpret_cast<uint4*>(orow)[i] = xv[j];
+        }
+      }
+      const float rn = rsqrtf(block_sum<T>(ss, red) / (float)N + eps);
+      T* yr = xn + m * ldn;
+#pragma unroll
+      for (int j = 0; j < kNormVec; ++j) {
+        const int i = threadIdx.x + j * kNormThreads;
+        if (i < nv) {
+          const T* e = reinterpret_cast<const T*>(&xv[j]);
+          const T* we = reinterpret_cast<const T*>(&wv[j]);
+          uint4 o;
+          T* oe = reinterpret_cast<T*>(&o);
+#pragma unroll
+          for (int t = 0; t < 8; ++t) oe[t] = from_f32<T>(to_f32<T>(we[t]) * round_to<T>(to_f32<T>(e[t]) * rn));
+          reinterpret_cast<uint4*>(yr)[i] = o;
+        }
+      }
+      __syncthreads();  // red is reused by the next row
+      continue;
+    }
+    for (int n = threadIdx.x; n < N; n += blockDim.x) {
+      float v = to_f32<T>(orow[n]);
+      for (int r = 0; r < G.n_ranks; ++r)
+        v = __fadd_rn(v, to_f32<T>(__ldcg(reinterpret_cast<const T*>(G.parts[r]) + part_offset + m * ld_p + n)));
+      orow[n] = from_f32<T>(v);
+    }
+    __syncthreads();  // the row is written: the norm's loads below see it
+    rmsnorm_row<T>(orow, w, xn + m * ldn, N, eps, red);
+    __syncthreads();
+  }
+  exchange_done(G, want);
 }
 
 }  // namespace
@@ -148,6 +262,34 @@ extern "C" int csaq_tp_exchange_sum(const csaq_p2p_group* group, int64_t part_of
                       reinterpret_cast<__nv_bfloat16*>(out), ldo, M, (int)N, spin);
   return launch_pdl(tp_exchange_kernel<__half>, dim3(grid), dim3(256), 0, st, G, part_offset, ld_parts,
                     reinterpret_cast<__half*>(out), ldo, M, (int)N, spin);
+}
+
+extern "C" int csaq_tp_exchange_sum_rmsnorm(const csaq_p2p_group* group, int64_t part_offset, int64_t ld_parts,
+                                            void* out, int64_t ldo, int64_t M, int64_t N, const void* norm_w,
+                                            void* xn, int64_t ldn, float eps, int dtype, void* stream) {
+  if (!group || !out || !norm_w || !xn || M < 0 || N <= 0 || ld_parts < N || ldo < N || ldn < N ||
+      part_offset < 0 || !(eps >= 0.0f))
+    return CSAQ_ERR_ARG;
+  const csaq_p2p_group& G = *group;
+  if (G.n_ranks < 1 || G.n_ranks > CSAQ_MAX_RANKS || G.rank < 0 || G.rank >= G.n_ranks || !G.seq || !G.ticket ||
+      !G.err)
+    return CSAQ_ERR_ARG;
+  for (int r = 0; r < G.n_ranks; ++r)
+    if (!G.parts[r] || !G.flags[r]) return CSAQ_ERR_ARG;
+  if (dtype != CSAQ_DT_F16 && dtype != CSAQ_DT_BF16) return CSAQ_ERR_ARG;
+  if (N > INT32_MAX) return CSAQ_ERR_UNSUPPORTED;
+  cudaStream_t st = as_stream(stream);
+  // one CTA per row, at most one wave; rows beyond it are taken in turn
+  const unsigned grid = (unsigned)(M < 1 ? 1 : (M > 128 ? 128 : M));
+  const long long spin = g_spin_limit.load();
+  if (dtype == CSAQ_DT_BF16)
+    return launch_pdl(tp_exchange_norm_kernel<__nv_bfloat16>, dim3(grid), dim3(kNormThreads), 0, st, G, part_offset,
+                      ld_parts, reinterpret_cast<__nv_bfloat16*>(out), ldo, M, (int)N,
+                      reinterpret_cast<const __nv_bfloat16*>(norm_w), reinterpret_cast<__nv_bfloat16*>(xn), ldn, eps,
+                      spin);
+  return launch_pdl(tp_exchange_norm_kernel<__half>, dim3(grid), dim3(kNormThreads), 0, st, G, part_offset, ld_parts,
+                    reinterpret_cast<__half*>(out), ldo, M, (int)N, reinterpret_cast<const __half*>(norm_w),
+                    reinterpret_cast<__half*>(xn), ldn, eps, spin);
 }
 
 extern "C" int csaq_p2p_set_spin_limit(int64_t polls) {

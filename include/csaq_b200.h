@@ -316,6 +316,14 @@ int csaq_ipc_close(void* ptr);
  * rank may rewrite a partial buffer only after the next exchange. */
 int csaq_tp_exchange_sum(const csaq_p2p_group* group, int64_t part_offset, int64_t ld_parts, void* out,
                          int64_t ldo, int64_t M, int64_t N, int dtype, void* stream);
+/* csaq_tp_exchange_sum followed by csaq_rmsnorm of its result in one launch
+ * (one CTA per row), bit for bit the two calls: out as above, then
+ * xn[m, :] = RMSNorm(out[m, :]) with weights norm_w (N values) and eps. For
+ * the combine after a row-split o/down projection that the next layer norm
+ * reads. */
+int csaq_tp_exchange_sum_rmsnorm(const csaq_p2p_group* group, int64_t part_offset, int64_t ld_parts,
+                                 void* out, int64_t ldo, int64_t M, int64_t N, const void* norm_w,
+                                 void* xn, int64_t ldn, float eps, int dtype, void* stream);
 int csaq_p2p_errors(const csaq_p2p_group* group, int64_t* count);
 /* Polls of a peer flag before csaq_tp_exchange_sum gives up its wait (default
  * 2^22, a few seconds), for launches made after the call (a captured graph
