@@ -239,9 +239,97 @@ __global__ void dequant_kernel(const uint8_t* __restrict__ p, const float* __res
   out[i] = from_f32<T>(w);
 }
 
+// The same dequantisation, eight consecutive columns of a row per thread:
+// one 2/4/8/16-byte code load, one scale and zero point, and 16- or 32-byte
+// stores, with 32-bit index arithmetic. Needs cols % 8 == 0, a group size that
+// is a multiple of 8 (or per-channel), and aligned buffers (csaq_dequant
+// checks). Column c + k of an octet is nibble k of the 4-bit word, bit pair k
+// of the 2-bit one, byte k of the 8-bit one and half k of the 16-bit one.
+template <typename T, int BITS>
+__global__ void dequant8_kernel(const uint8_t* __restrict__ p, const float* __restrict__ s,
+                                const int32_t* __restrict__ z, int rows, int octs, int gs_oct, int n_groups,
+                                int64_t row_bytes, int nan_to_num, T* __restrict__ out) {
+  const int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i >= int64_t(rows) * octs) return;
+  const int r = (int)(i / octs), o = (int)(i - int64_t(r) * octs);
+  const uint8_t* rp = p + int64_t(r) * row_bytes;
+  float w[8];
+  if constexpr (BITS == 16) {
+    const uint4 v = reinterpret_cast<const uint4*>(rp)[o];
+    const __half* h = reinterpret_cast<const __half*>(&v);
+#pragma unroll
+    for (int k = 0; k < 8; ++k) w[k] = __half2float(h[k]);
+  } else {
+    const int g = gs_oct ? o / gs_oct : 0;
+    const float sc = s[int64_t(r) * n_groups + g];
+    const int32_t zp = z[int64_t(r) * n_groups + g];
+    int32_t q[8];
+    if constexpr (BITS == 8) {
+      const uint2 v = reinterpret_cast<const uint2*>(rp)[o];
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        q[k] = (v.x >> (8 * k)) & 0xFF;
+        q[k + 4] = (v.y >> (8 * k)) & 0xFF;
+      }
+    } else if constexpr (BITS == 4) {
+      const uint32_t v = reinterpret_cast<const uint32_t*>(rp)[o];
+#pragma unroll
+      for (int k = 0; k < 8; ++k) q[k] = (v >> (4 * k)) & 0xF;
+    } else {
+      const uint32_t v = reinterpret_cast<const uint16_t*>(rp)[o];
+#pragma unroll
+      for (int k = 0; k < 8; ++k) q[k] = (v >> (2 * k)) & 0x3;
+    }
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      float x = dequant_one(q[k], zp, sc);
+      if (nan_to_num) {
+        if (x != x) x = 0.0f;
+        else if (x == INFINITY) x = 65504.0f;
+        else if (x == -INFINITY) x = -65504.0f;
+      }
+      w[k] = x;
+    }
+  }
+  T* dst = out + int64_t(r) * octs * 8 + int64_t(o) * 8;
+  if constexpr (sizeof(T) == 4) {
+    reinterpret_cast<float4*>(dst)[0] = make_float4(w[0], w[1], w[2], w[3]);
+    reinterpret_cast<float4*>(dst)[1] = make_float4(w[4], w[5], w[6], w[7]);
+  } else {
+    uint4 v;
+    T* e = reinterpret_cast<T*>(&v);
+#pragma unroll
+    for (int k = 0; k < 8; ++k) e[k] = from_f32<T>(w[k]);
+    *reinterpret_cast<uint4*>(dst) = v;
+  }
+}
+
 inline int64_t blocks_for(int64_t n) { return (n + kThreads - 1) / kThreads; }
 
 inline bool is_per_channel(int64_t gs, int64_t cols) { return gs <= 0 || gs >= cols; }
+
+template <typename T>
+int launch_dequant8_t(const uint8_t* q, const float* s, const int32_t* z, int bits, int rows, int octs, int gs_oct,
+                      int n_groups, int64_t rb, int nan, T* out, cudaStream_t st) {
+  const int64_t blocks = blocks_for(int64_t(rows) * octs);
+  switch (bits) {
+    case 16: dequant8_kernel<T, 16><<<blocks, kThreads, 0, st>>>(q, s, z, rows, octs, gs_oct, n_groups, rb, nan, out); break;
+    case 8: dequant8_kernel<T, 8><<<blocks, kThreads, 0, st>>>(q, s, z, rows, octs, gs_oct, n_groups, rb, nan, out); break;
+    case 4: dequant8_kernel<T, 4><<<blocks, kThreads, 0, st>>>(q, s, z, rows, octs, gs_oct, n_groups, rb, nan, out); break;
+    default: dequant8_kernel<T, 2><<<blocks, kThreads, 0, st>>>(q, s, z, rows, octs, gs_oct, n_groups, rb, nan, out); break;
+  }
+  return launch_status();
+}
+
+int launch_dequant8(const uint8_t* q, const float* s, const int32_t* z, int bits, int rows, int octs, int gs_oct,
+                    int n_groups, int64_t rb, int nan, int out_dtype, void* out, cudaStream_t st) {
+  if (out_dtype == CSAQ_DT_F32)
+    return launch_dequant8_t(q, s, z, bits, rows, octs, gs_oct, n_groups, rb, nan, reinterpret_cast<float*>(out), st);
+  if (out_dtype == CSAQ_DT_F16)
+    return launch_dequant8_t(q, s, z, bits, rows, octs, gs_oct, n_groups, rb, nan, reinterpret_cast<__half*>(out), st);
+  return launch_dequant8_t(q, s, z, bits, rows, octs, gs_oct, n_groups, rb, nan,
+                           reinterpret_cast<__nv_bfloat16*>(out), st);
+}
 
 }  // namespace
 }  // namespace csaq
@@ -377,6 +465,12 @@ extern "C" int csaq_dequant(const uint8_t* qdata, const float* scales, const int
   const int64_t rb = packed_row_bytes(cols, bits);
   const int64_t n = rows * cols;
   cudaStream_t st = as_stream(stream);
+  const int align = bits == 16 ? 16 : bits;  // bytes of one octet's codes
+  if (cols % 8 == 0 && (gs == 0 || gs % 8 == 0) && rows <= INT32_MAX && cols / 8 <= INT32_MAX &&
+      n_groups <= INT32_MAX && reinterpret_cast<uintptr_t>(qdata) % align == 0 &&
+      reinterpret_cast<uintptr_t>(out) % 16 == 0)
+    return launch_dequant8(qdata, scales, zero_points, bits, (int)rows, (int)(cols / 8), (int)(gs / 8),
+                           (int)n_groups, rb, nan_to_num, out_dtype, out, st);
   switch (out_dtype) {
     case CSAQ_DT_F32:
       dequant_kernel<float><<<blocks_for(n), kThreads, 0, st>>>(qdata, scales, zero_points, bits, rows, cols, gs, n_groups, rb, nan_to_num, reinterpret_cast<float*>(out));
