@@ -11,10 +11,8 @@
 //     c*32 .. c*32+31, followed by the tile's 16 fp32 scales and 16 uint8 zero
 //     points. 8-bit rows are stored as two 4-bit planes (low and high nibbles);
 //     fp16 rows are stored pre-arranged in the 4-bit column order (values in
-//     "high" positions times 16, exact), the chunk's first two k-steps before
-//     its last two, so that each half is a work item of its own (2 KB, like
-//     a 4-bit item: every warp's ring keeps about as many bytes in flight).
-//   * Work = (unit, chunk) items (fp16: (unit, half chunk)) of every tier of the launch, spread over the
+//     "high" positions times 16, exact).
+//   * Work = (unit, chunk) items of every tier of the launch, spread over the
 //     warps of a one-CTA-per-SM grid of 2-CTA clusters: each cluster takes a
 //     run of whole units, cut so the clusters carry equal cost (measured time
 //     per item by bit-width), and
@@ -118,7 +116,7 @@ __global__ void repack_codes_kernel(const csaq_tier T, int64_t n_chunks, int64_t
   const int g = lane >> 2, c = lane & 3;
   int h, q = 0, plane = 0;
   if (bits == 8) { plane = p / 64; h = (p / 32) % 2; }
-  else if (bits == 16) { h = (p / 64) % 2; q = 2 * (p / 128) + (p / 32) % 2; }  // [k-step pair][row half][k-step][lane]
+  else if (bits == 16) { h = p / 128; q = (p / 32) % 4; }
   else { h = p / 32; }
   const int64_t tile = unit * mt_n + mt;
   const int64_t row = tile * kTileRows + g + 8 * h;
@@ -279,10 +277,9 @@ __device__ __forceinline__ void mma2(const uint32_t (&cw)[2][2][2], const uint2 
 }
 
 // 16-bit (pre-arranged fp16): words [4m], [4m+1] with rec[2m]; [4m+2], [4m+3] with rec[2m+1]
-// fp16 rows, one half of a chunk (two of its four k-steps; rec holds their records)
-__device__ __forceinline__ void mma16(const uint32_t (&cw)[2][8], const uint2 (&rec)[8], float (&g)[2][4]) {
+__device__ __forceinline__ void mma16(const uint32_t (&cw)[2][16], const uint2 (&rec)[8], float (&g)[2][4]) {
 #pragma unroll
-  for (int m = 0; m < 2; ++m) {
+  for (int m = 0; m < 4; ++m) {
     mma_f16(g[0], cw[0][4 * m], cw[1][4 * m], cw[0][4 * m + 1], cw[1][4 * m + 1], rec[2 * m].x, rec[2 * m].y);
     mma_f16(g[1], cw[0][4 * m + 2], cw[1][4 * m + 2], cw[0][4 * m + 3], cw[1][4 * m + 3], rec[2 * m + 1].x,
             rec[2 * m + 1].y);
@@ -301,7 +298,7 @@ constexpr int kMaxWarps = kMaxCtas * 16;
 struct TierWork {
   int bits, mt, n_units;
   int item0;    // first item of the tier
-  int n_items;  // n_units * n_chunks * items_per_chunk(bits)
+  int n_items;  // n_units * n_chunks
 };
 
 struct KParams {
@@ -309,7 +306,7 @@ struct KParams {
   TierWork w[CSAQ_MAX_TIERS];
   int n_items_total;
   int n_warps;     // W = gridDim.x * kWarps
-  int slot_bytes;  // ring slot: the largest item_bytes of the launch
+  int slot_bytes;  // ring slot: the largest chunk_bytes of the launch
   int depth;       // ring slots per warp
   int want2;       // any 2-bit tier (stage R2 records)
   int x_bytes;     // R4 records: n_rec * M * kRecStride (R2 the same again when want2)
@@ -453,16 +450,12 @@ __device__ __forceinline__ float ld_dsmem_f32_after_sync(uint32_t addr) {
 // DS: the chunk's records and (C, S) live in the other CTA of the cluster
 // (or this one) and are read through distributed shared memory at the
 // shared::cluster addresses rb_cl and xcs_cl; otherwise at rbase and xcs_ch.
-// sub: for fp16 tiers the half of the chunk the slot holds (its k-steps
-// 2 sub and 2 sub + 1); 0 otherwise.
 template <int BITS, int NT, bool DS>
 __device__ __forceinline__ void chunk_math(const uint8_t* slot, const uint8_t* rbase,
                                            const float4* xcs_ch, uint32_t rb_cl, uint32_t xcs_cl, int M,
-                                           int lane, int sub, float (&acc)[2][NT][4]) {
+                                           int lane, float (&acc)[2][NT][4]) {
   constexpr int bits = BITS;
-  constexpr int NQ = bits == 16 ? 4 : 8;  // records a lane needs: 2 per k-step
   const int g = lane >> 2, c = lane & 3;
-  const int q0 = bits == 16 ? 4 * sub : 0;
 #pragma unroll
   for (int nt = 0; nt < NT; ++nt) {
     const int tok = nt * 8 + g;
@@ -471,14 +464,14 @@ __device__ __forceinline__ void chunk_math(const uint8_t* slot, const uint8_t* r
       if constexpr (DS) {
         const uint32_t ra = rb_cl + (uint32_t)(tok * kRecStride + 8 * c);
 #pragma unroll
-        for (int q = 0; q < NQ; ++q)
+        for (int q = 0; q < 8; ++q)
           asm volatile("ld.shared::cluster.v2.u32 {%0, %1}, [%2];"
                        : "=r"(rec[q].x), "=r"(rec[q].y)
-                       : "r"(ra + 32u * (uint32_t)(q0 + q)));
+                       : "r"(ra + 32u * q));
       } else {
         const uint2* rp = reinterpret_cast<const uint2*>(rbase + tok * kRecStride) + c;
 #pragma unroll
-        for (int q = 0; q < NQ; ++q) rec[q] = rp[4 * (q0 + q)];
+        for (int q = 0; q < 8; ++q) rec[q] = rp[4 * q];
       }
     } else {
 #pragma unroll
@@ -546,15 +539,14 @@ __device__ __forceinline__ void chunk_math(const uint8_t* slot, const uint8_t* r
         acc[0][nt][3] = fmaf(s1 * cs1.w, fmaf(-z1, cs1.y, d[3]), acc[0][nt][3]);
       }
     } else if constexpr (bits == 16) {
-      // the half-block: [row half h][k-step of the pair][lane], 16 bytes each
-      uint32_t cw[2][8];
+      uint32_t cw[2][16];
       float gg[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
       const uint4* cp = reinterpret_cast<const uint4*>(slot);
 #pragma unroll
       for (int h = 0; h < 2; ++h)
 #pragma unroll
-        for (int q = 0; q < 2; ++q) {
-          const uint4 v = cp[(h * 2 + q) * 32 + lane];
+        for (int q = 0; q < 4; ++q) {
+          const uint4 v = cp[(h * 4 + q) * 32 + lane];
           cw[h][4 * q] = v.x; cw[h][4 * q + 1] = v.y; cw[h][4 * q + 2] = v.z; cw[h][4 * q + 3] = v.w;
         }
       mma16(cw, rec, gg);
@@ -638,7 +630,7 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kThreads, 1)
   int i_cb = 0, i_n = 0;
   auto enter_tier = [&]() {
     i_blocks = P.tp.t[i_t].blocks;
-    i_cb = item_bytes(P.w[i_t].bits);
+    i_cb = chunk_bytes(P.w[i_t].bits);
     i_n = P.w[i_t].n_items;
   };
   const int slot_bytes = P.slot_bytes, depth = P.depth;
@@ -754,11 +746,9 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kThreads, 1)
     t = tier_of_item(P, item);
     local = item - P.w[t].item0;
   }
-  // items [s_first, s_last) of a unit: chunk s (fp16: half s % 2 of chunk s / 2)
-  auto chunks = [&](auto bits_c, int s_first, int s_last) {
+  auto chunks = [&](auto bits_c, int ch_first, int ch_last) {
     constexpr int B = decltype(bits_c)::value;
-    for (int s = s_first; s < s_last; ++s) {
-      const int ch = B == 16 ? s >> 1 : s, sub = B == 16 ? (s & 1) : 0;
+    for (int ch = ch_first; ch < ch_last; ++ch) {
       if (!mbar_wait(&bars[c_slot], (phase >> c_slot) & 1u)) {
         late |= 1u << c_slot;
         late_parity = (late_parity & ~(1u << c_slot)) | (phase & (1u << c_slot));
@@ -768,10 +758,10 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kThreads, 1)
         const int r = ch >= P.ch_half ? 1 : 0, li = ch - r * P.ch_half;
         const uint32_t rb = dsmem_addr(smem_u32((B == 2 ? rec2 : rec4) + (int64_t)li * M * kRecStride), r);
         const uint32_t xb = dsmem_addr(smem_u32(xcs + li * M), r);
-        chunk_math<B, NT, true>(ring + c_slot * P.slot_bytes, nullptr, nullptr, rb, xb, M, lane, sub, acc);
+        chunk_math<B, NT, true>(ring + c_slot * P.slot_bytes, nullptr, nullptr, rb, xb, M, lane, acc);
       } else {
         chunk_math<B, NT, false>(ring + c_slot * P.slot_bytes, (B == 2 ? rec2 : rec4) + (int64_t)ch * M * kRecStride,
-                                 xcs + ch * M, 0u, 0u, M, lane, sub, acc);
+                                 xcs + ch * M, 0u, 0u, M, lane, acc);
       }
       __syncwarp();
       issue();
@@ -779,20 +769,19 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kThreads, 1)
     }
   };
   // the current tier's work fields, reloaded only at tier boundaries
-  int c_bits = 0, c_mt = 0, c_item0 = 0, c_n = 0, c_ipu = 0;
+  int c_bits = 0, c_mt = 0, c_item0 = 0, c_n = 0;
   auto enter_ctier = [&]() {
     c_bits = P.w[t].bits;
     c_mt = P.w[t].mt;
     c_item0 = P.w[t].item0;
     c_n = P.w[t].n_items;
-    c_ipu = n_chunks * items_per_chunk(c_bits);  // items per unit
   };
   if (item < it_end) enter_ctier();
   while (item < it_end) {
-    const int unit = local / c_ipu;
-    const int ch_first = local - unit * c_ipu;
+    const int unit = local / n_chunks;
+    const int ch_first = local - unit * n_chunks;
     const int room = it_end - item;
-    const int ch_last = room < c_ipu - ch_first ? ch_first + room : c_ipu;
+    const int ch_last = room < n_chunks - ch_first ? ch_first + room : n_chunks;
 #pragma unroll
     for (int a = 0; a < 2; ++a)
 #pragma unroll
@@ -804,8 +793,8 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kThreads, 1)
       default: chunks(std::integral_constant<int, 2>(), ch_first, ch_last); break;
     }
 
-    const int u_start = c_item0 + unit * c_ipu;
-    if (ch_first == 0 && ch_last == c_ipu) {
+    const int u_start = c_item0 + unit * n_chunks;
+    if (ch_first == 0 && ch_last == n_chunks) {
       // the whole unit is in this warp: write y from the fragments
       const csaq_tier& T = P.tp.t[t];
 #pragma unroll
@@ -845,7 +834,6 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kThreads, 1)
   const int b_lane = pin(P.begin[cl_base + lane]), b_end = pin(P.begin[cl_base + 32]);
   const int t_own = cut_t0 >= 0 ? cut_t0 : 0;
   const int own_rows = pin(P.w[t_own].mt) * kTileRows;
-  const int own_ipu = n_chunks * items_per_chunk(pin(P.w[t_own].bits));  // items per unit
   const bool own_silu = (P.silu_tiers >> t_own) & 1u;
   OutDesc od;
   od.out_rows = pin(P.tp.t[t_own].out_rows);
@@ -895,7 +883,7 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kThreads, 1)
   // Only a warp's first unit can be one it finishes: its last unit, when cut,
   // continues in a higher warp. The finishing (highest) warp of a cut unit
   // adds the partials in warp order and writes y.
-  const int u_start = cut_s0, u_end = cut_s0 + own_ipu;
+  const int u_start = cut_s0, u_end = cut_s0 + n_chunks;
   const bool own = cut_t0 >= 0 && begin_of(wg + 1) >= u_end;  // units never cross a cluster boundary
   float v[16];
 #pragma unroll
@@ -1085,8 +1073,8 @@ int64_t work_table(const TierParams& TP, int64_t K, TierWork* w) {
     w[i].mt = mt;
     w[i].n_units = (int)units;
     w[i].item0 = (int)items;
-    w[i].n_items = (int)(units * n_chunks * items_per_chunk(t.bits));
-    items += units * n_chunks * items_per_chunk(t.bits);
+    w[i].n_items = (int)(units * n_chunks);
+    items += units * n_chunks;
   }
   return items >= (int64_t)1 << 30 ? -1 : items;
 }
@@ -1106,13 +1094,12 @@ struct PartitionCache {
   size_t next = 0;
 };
 
-// Relative time of one item by bit-width, as measured on B200 with every warp
-// streaming: a whole 16-bit chunk (16 rows, 4 KB) takes about 0.7-0.8 of a
-// 4-bit item (a chunk of 32 rows, 2.2 KB), so each of its two half-chunk items
-// is costed at 0.41; an 8-bit item (16 rows as two nibble planes) takes about
-// as long as a 4-bit one. Warps streaming fp16 rows finish early when items
-// are costed by bytes.
-int64_t item_cost(int bits) { return bits == 16 ? 41 : (bits == 8 ? 100 : 100); }
+// Relative time of one item (a unit's 128-column chunk) by bit-width, as
+// measured on B200 with every warp streaming: a 16-bit item (16 rows, 4 KB)
+// takes about 0.8 of a 4-bit item (32 rows, 2.2 KB), an 8-bit one (16 rows as
+// two nibble planes) about as long as a 4-bit one. Warps streaming fp16 rows
+// finish early when items are costed by bytes.
+int64_t item_cost(int bits) { return bits == 16 ? 82 : (bits == 8 ? 100 : 100); }
 
 bool partition(const TierParams& TP, const TierWork* w, int64_t K, int n_warps, int* begin) {
   static PartitionCache cache;
@@ -1163,11 +1150,10 @@ bool partition(const TierParams& TP, const TierWork* w, int64_t K, int n_warps, 
     const int64_t target = total * j / n_clusters;
     int t = 0;
     while (t + 1 < n_tiers && target >= cost0[t + 1]) ++t;
-    const int64_t ipu = n_chunks * items_per_chunk(w[t].bits);  // items per unit
-    const int64_t unit_cost = ic[t] * ipu;
+    const int64_t unit_cost = ic[t] * n_chunks;
     int64_t u = unit_cost > 0 ? (target - cost0[t] + unit_cost / 2) / unit_cost : 0;
     if (u > w[t].n_units) u = w[t].n_units;
-    int item = w[t].item0 + (int)(u * ipu);
+    int item = w[t].item0 + (int)(u * n_chunks);
     if (item < cb[j - 1]) item = cb[j - 1];
     if (item > n_items) item = n_items;
     cb[j] = item;
@@ -1199,7 +1185,7 @@ bool make_plan(const TierParams& TP, int64_t K, int M, Plan& p) {
   p.want2 = 0;
   for (int i = 0; i < TP.n_tiers; ++i) {
     if (TP.t[i].n_rows == 0) continue;
-    const int cb = item_bytes(TP.t[i].bits);
+    const int cb = chunk_bytes(TP.t[i].bits);
     p.slot_bytes = cb > p.slot_bytes ? cb : p.slot_bytes;
     if (TP.t[i].bits == 2) p.want2 = 1;
   }

@@ -2,9 +2,7 @@
 // per (unit, 128-column chunk), unit-major; a unit is 2 tiles of 16 rows for
 // 2- and 4-bit tiers and 1 tile otherwise. Inside a block, tile mt starts at
 // mt * tile_block_bytes: its codes (code_bytes), then the 16 rows' fp32 scales
-// (64 B) and uint8 zero points (16 B) of the chunk's group. An fp16 block has
-// no metadata: its first 2048 bytes hold the operands of the chunk's first two
-// 32-column MMA k-steps, the next 2048 bytes those of the last two.
+// (64 B) and uint8 zero points (16 B) of the chunk's group.
 #pragma once
 
 namespace csaq {
@@ -20,13 +18,6 @@ __host__ __device__ __forceinline__ constexpr int tile_block_bytes(int bits) {
 }
 __host__ __device__ __forceinline__ constexpr int chunk_bytes(int bits) {  // one unit x one chunk
   return unit_tiles(bits) * tile_block_bytes(bits);
-}
-// A work item of the tensor-core GEMV is one (unit, chunk) block, or for fp16
-// tiers one half of it (two of the chunk's four k-steps, 2048 bytes), so an
-// fp16 item is as small as the others and every ring slot fits in about 2 KB.
-__host__ __device__ __forceinline__ constexpr int items_per_chunk(int bits) { return bits == 16 ? 2 : 1; }
-__host__ __device__ __forceinline__ constexpr int item_bytes(int bits) {
-  return chunk_bytes(bits) / items_per_chunk(bits);
 }
 
 }  // namespace csaq

@@ -149,8 +149,7 @@ typedef struct csaq_tier {
 /* GEMV block layout of a tier: one contiguous block per (16-row tile,
  * 128-column chunk), tile-major; inside a block the codes are ordered by the
  * MMA lane that consumes them, followed by the 16 rows' fp32 scales and uint8
- * zero points of that chunk's group (rows past n_rows are zero); an fp16
- * block holds the chunk's first two MMA k-steps, then its last two. Built once
+ * zero points of that chunk's group (rows past n_rows are zero). Built once
  * per layer from the reference layout; K must be a multiple of 128 and the
  * group size a power-of-two multiple of 128 (or per-channel). */
 int64_t csaq_tile_blocks_bytes(int bits, int64_t n_rows, int64_t K);
