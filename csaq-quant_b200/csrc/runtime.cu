@@ -120,6 +120,13 @@ constexpr int kChunk = 64;
 constexpr int kAttnWarps = 16;
 constexpr int kMergeBatch = 16;  // partials whose loads are issued together in the merge
 constexpr int kKeyBlock = 8;     // keys scored together: independent dot products, one shuffle tree
+// With up to kGroupRowsMax query rows, each row's chunk is scored as
+// kKeyGroups groups of kChunk / kKeyGroups keys by different warps (a warp per
+// (row, group)), whose partial states meet in shared memory and are combined
+// in group order: the 16 warps share the work of a few rows.
+constexpr int kKeyGroups = 4;
+constexpr int kGroupRowsMax = 32;
+__host__ __device__ constexpr int key_groups(int R) { return R <= kGroupRowsMax ? kKeyGroups : 1; }
 
 // ROPE: the launch also does csaq_rope_kv's work for the step's tokens (same
 // expressions, so the same bits): q holds the unrotated queries (rows ldq
@@ -253,18 +260,23 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attention_kernel(
   __syncthreads();
   // partial layout: [bh][sp][r][D + 2]
   float* pbase = part + ((int64_t)bh * n_split + sp) * R * (D + 2);
-  for (int r = warp; r < R; r += kAttnWarps) {
+  const int NG = key_groups(R), kq = kChunk / NG;
+  // with NG > 1: the groups' states [r][g][D + 2], after the staged query rows
+  float* gpart = reinterpret_cast<float*>(attn_dyn + ((int64_t)R * D * sizeof(T) + 15) / 16 * 16);
+  for (int task = warp; task < R * NG; task += kAttnWarps) {
+    const int r = task / NG, grp = task - r * NG;
     const int s = r / G;
     const int qpos = p0 + s;  // attends keys 0..qpos
     float qv[E];
 #pragma unroll
     for (int i = 0; i < E; ++i) qv[i] = to_f32<T>(qs[(int64_t)r * D + lane * E + i]) * scale;
     const int kmax = min(n_keys, qpos - k0 + 1);
+    const int j0 = grp * kq, j1 = min(kmax, j0 + kq);  // this group's keys
     float m = -INFINITY, l = 0.0f, o[E];
 #pragma unroll
     for (int i = 0; i < E; ++i) o[i] = 0.0f;
-    int j = 0;
-    for (; j + kKeyBlock <= kmax; j += kKeyBlock) {  // a block of keys: independent dot products
+    int j = j0;
+    for (; j + kKeyBlock <= j1; j += kKeyBlock) {  // a block of keys: independent dot products
       float d[kKeyBlock];
 #pragma unroll
       for (int t = 0; t < kKeyBlock; ++t) {
@@ -296,7 +308,7 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attention_kernel(
       }
       m = mn;
     }
-    for (; j < kmax; ++j) {
+    for (; j < j1; ++j) {
       float d = 0.0f;
 #pragma unroll
       for (int i = 0; i < E; ++i) d = fmaf(qv[i], to_f32<T>(ks[j][lane * E + i]), d);
@@ -309,10 +321,36 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attention_kernel(
       for (int i = 0; i < E; ++i) o[i] = fmaf(o[i], corr, p * to_f32<T>(vs[j][lane * E + i]));
       m = mn;
     }
-    float* pr = pbase + (int64_t)r * (D + 2);
+    float* pr = NG == 1 ? pbase + (int64_t)r * (D + 2) : gpart + (int64_t)task * (D + 2);
 #pragma unroll
     for (int i = 0; i < E; ++i) pr[lane * E + i] = o[i];
     if (lane == 0) { pr[D] = m; pr[D + 1] = l; }
+  }
+  if (NG > 1) {
+    __syncthreads();
+    // the chunk's state of each row from its groups, in group order; a group
+    // without keys holds m = -inf, l = 0, o = 0 (weight 0), and a row without
+    // keys in this chunk keeps that state
+    for (int r = warp; r < R; r += kAttnWarps) {
+      const float* gp = gpart + (int64_t)r * NG * (D + 2);
+      float M_ = -INFINITY;
+      for (int g = 0; g < NG; ++g) M_ = fmaxf(M_, gp[g * (D + 2) + D]);
+      float L = 0.0f, o[E];
+#pragma unroll
+      for (int i = 0; i < E; ++i) o[i] = 0.0f;
+      if (M_ != -INFINITY) {
+        for (int g = 0; g < NG; ++g) {
+          const float w = __expf(gp[g * (D + 2) + D] - M_);
+          L = fmaf(gp[g * (D + 2) + D + 1], w, L);
+#pragma unroll
+          for (int i = 0; i < E; ++i) o[i] = fmaf(gp[g * (D + 2) + lane * E + i], w, o[i]);
+        }
+      }
+      float* pr = pbase + (int64_t)r * (D + 2);
+#pragma unroll
+      for (int i = 0; i < E; ++i) pr[lane * E + i] = o[i];
+      if (lane == 0) { pr[D] = M_; pr[D + 1] = L; }
+    }
   }
   __threadfence();
   __syncthreads();
@@ -600,7 +638,9 @@ static int launch_attention(int64_t D, dim3 grid, cudaStream_t st, const void* q
                             int64_t Lmax, float scale, float* part, int32_t* tickets, void* out,
                             const RopeArgs& ra = RopeArgs{}) {
   auto kern = D == 64 ? attention_kernel<T, 64, ROPE> : attention_kernel<T, 128, ROPE>;
-  int64_t qbytes = S * (Hq / Hkv) * D * (int64_t)sizeof(T);
+  const int64_t R = S * (Hq / Hkv);
+  int64_t qbytes = (R * D * (int64_t)sizeof(T) + 15) / 16 * 16;  // the staged query rows
+  if (R <= kGroupRowsMax) qbytes += R * key_groups((int)R) * (D + 2) * (int64_t)sizeof(float);  // group states
   if (qbytes > kAttnQBytesMax) return CSAQ_ERR_UNSUPPORTED;
   // spread only a grid that fits one wave: a larger one (many sequences) keeps
   // several CTAs per SM rather than running wave after wave
