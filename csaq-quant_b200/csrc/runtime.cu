@@ -361,15 +361,19 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attention_kernel(
   __threadfence();
   // merge, in chunk order: an empty chunk left m = -inf, l = 0, o = 0, whose
   // weight exp(-inf - M) is 0, so every chunk is added without a branch on the
-  // loaded values and the loads of a batch go out together
+  // loaded values and the loads of a batch go out together; with at most one
+  // batch of chunks the maxima come from the same loads (one round trip)
   for (int r = warp; r < R; r += kAttnWarps) {
     const int s = r / G, hq = h * G + r % G;
     const float* prow = part + ((int64_t)bh * n_split * R + r) * (D + 2);  // chunk p at + p * R * (D + 2)
     const int64_t pstride = (int64_t)R * (D + 2);
-    float M_ = -INFINITY;  // the maxima, lane-parallel (a maximum is exact in any order)
-    for (int p = lane; p < n_split; p += 32) M_ = fmaxf(M_, __ldcg(prow + p * pstride + D));
+    float M_ = -INFINITY;  // the maxima (a maximum is exact in any order)
+    const bool one_batch = n_split <= kMergeBatch;
+    if (!one_batch) {  // lane-parallel first; one batch finds them among its own loads
+      for (int p = lane; p < n_split; p += 32) M_ = fmaxf(M_, __ldcg(prow + p * pstride + D));
 #pragma unroll
-    for (int off = 16; off > 0; off >>= 1) M_ = fmaxf(M_, __shfl_xor_sync(0xffffffffu, M_, off));
+      for (int off = 16; off > 0; off >>= 1) M_ = fmaxf(M_, __shfl_xor_sync(0xffffffffu, M_, off));
+    }
     float L = 0.0f, o[E];
 #pragma unroll
     for (int i = 0; i < E; ++i) o[i] = 0.0f;
@@ -383,6 +387,10 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attention_kernel(
         lb[u] = ok ? __ldcg(pr + D + 1) : 0.0f;
 #pragma unroll
         for (int i = 0; i < E; ++i) ob[u][i] = ok ? __ldcg(pr + lane * E + i) : 0.0f;
+      }
+      if (one_batch) {
+#pragma unroll
+        for (int u = 0; u < kMergeBatch; ++u) M_ = fmaxf(M_, mb[u]);
       }
 #pragma unroll
       for (int u = 0; u < kMergeBatch; ++u) {
