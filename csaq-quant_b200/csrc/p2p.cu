@@ -84,8 +84,8 @@ __device__ __forceinline__ void exchange_done(const csaq_p2p_group& G, uint64_t 
 template <typename T>
 __global__ void tp_exchange_kernel(const csaq_p2p_group G, int64_t part_offset, int64_t ld_p, T* __restrict__ out,
                                    int64_t ldo, int64_t M, int N, long long spin_limit) {
-  pdl_wait();  // this rank's partial, written by the previous kernel, is complete
   pdl_trigger();
+  pdl_wait();  // this rank's partial, written by the previous kernel, is complete
   const uint64_t want = exchange_signal_wait(G, spin_limit);
   for (int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; i < M * N; i += int64_t(gridDim.x) * blockDim.x) {
     const int64_t m = i / N, n = i - m * N;
@@ -107,8 +107,8 @@ __global__ void __launch_bounds__(kNormThreads)
     tp_exchange_norm_kernel(const csaq_p2p_group G, int64_t part_offset, int64_t ld_p, T* __restrict__ out,
                             int64_t ldo, int64_t M, int N, const T* __restrict__ w, T* __restrict__ xn,
                             int64_t ldn, float eps, long long spin_limit) {
-  pdl_wait();
   pdl_trigger();
+  pdl_wait();
   const uint64_t want = exchange_signal_wait(G, spin_limit);
   __shared__ float red[32];
   const bool vec = N % 8 == 0 && N <= kNormThreads * 8 * kNormVec && ldo % 8 == 0 && ldn % 8 == 0 &&

@@ -22,8 +22,8 @@ template <typename T>
 __global__ void __launch_bounds__(kNormThreads) rmsnorm_kernel(const T* __restrict__ x, int64_t ldx,
                                                                const T* __restrict__ w, T* __restrict__ y,
                                                                int64_t ldy, int H, float eps) {
+  pdl_trigger();  // the next kernel may launch now; it waits for this one before reading y
   pdl_wait();
-  pdl_trigger();
   __shared__ float red[32];
   const int64_t row = blockIdx.x;
   rmsnorm_row<T>(x + row * ldx, w, y + row * ldy, H, eps, red);
@@ -184,11 +184,13 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attention_kernel(
   const int bh = blockIdx.x, sp = blockIdx.y, n_split = gridDim.y;
   const int b = bh / Hkv, h = bh % Hkv;
   const int G = Hq / Hkv, R = S * G;
-  // pos0 and the cache below pos0 were written steps ago, by kernels that
-  // finished before the one this launch may overlap (which waits for its own
-  // predecessor before it lets this one start): the chunk's old keys and
-  // values are copied before waiting, the new ones (written by the
-  // predecessor) after
+  pdl_trigger();  // the next kernel may launch now; it waits for this one before reading out
+  // pos0 and the cache below pos0 were written before the step began (by the
+  // host-ordered position update and by this layer's attention of earlier
+  // steps); only the kernels of the current layer, which start once their
+  // predecessor's CTAs are all running, can still be in flight: the chunk's
+  // old keys and values are copied before waiting, the new ones (from the
+  // predecessor's q/k/v) after
   const int p0 = pos0[b];
   // every CTA of this head sees the same p0, so all of them skip together and
   // the merge ticket stays consistent
@@ -209,7 +211,6 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attention_kernel(
     cp_async16(reinterpret_cast<uint4*>(&vs[0][0]) + e, reinterpret_cast<const uint4*>(vb) + e);
   }
   pdl_wait();
-  pdl_trigger();
   if constexpr (ROPE) {
     // the chunk's new positions: rotated keys and copied values, into shared
     // memory and the cache (work items as csaq_rope_kv: 8 rotary pairs, or one
@@ -451,8 +452,8 @@ template <typename T>
 __global__ void __launch_bounds__(kArgThreads) argmax_kernel(const T* __restrict__ logits, int n_parts,
                                                              int64_t part_stride, int64_t ld, int64_t part_len,
                                                              int64_t* __restrict__ idx) {
-  pdl_wait();
   pdl_trigger();
+  pdl_wait();
   const int64_t m = blockIdx.x;
   float best = -INFINITY;
   int64_t bi = INT64_MAX;
