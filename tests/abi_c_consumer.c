@@ -2,6 +2,7 @@
  * header compiles without C++ and the shared library links and answers
  * host-side calls (identification, sizes, argument validation) with no GPU.
  * Built and run by tests/test_abi_cpu.py. Prints one line per check. */
+#include <stddef.h>
 #include <stdio.h>
 #include <stdint.h>
 
@@ -29,5 +30,11 @@ int main(void) {
   printf("greedy_null %d\n", csaq_greedy_cliques(NULL, 1, 1, NULL, NULL, NULL));
   int64_t n = -1, site = -1, value = -1, bound = -1;
   printf("checked %d guard %d\n", csaq_checked_build(), csaq_guard_report(&n, &site, &value, &bound));
+  /* struct layouts, compared with the Python binding's ctypes mirrors */
+  printf("layout_tier %u %u %u %u\n", (unsigned)sizeof(csaq_tier), (unsigned)offsetof(csaq_tier, blocks),
+         (unsigned)offsetof(csaq_tier, y), (unsigned)offsetof(csaq_tier, ldr));
+  printf("layout_gemv_ext %u %u\n", (unsigned)sizeof(csaq_gemv_ext), (unsigned)offsetof(csaq_gemv_ext, x_mul));
+  printf("layout_p2p_group %u %u %u\n", (unsigned)sizeof(csaq_p2p_group), (unsigned)offsetof(csaq_p2p_group, flags),
+         (unsigned)offsetof(csaq_p2p_group, err));
   return 0;
 }

@@ -103,6 +103,12 @@ def test_c_consumer_compiles_links_and_runs(tmp_path):
     assert lines["qgemv_bits"] == "-2" and lines["qgemv_tiers"] == "-1"
     assert lines["greedy_null"] == "-1"
     assert lines["checked"] == "0 guard -5"
+    # the ctypes mirrors of the ABI structs have the C layout
+    from csaq import _lib
+    T, E, G = _lib.CsaqTier, _lib.CsaqGemvExt, _lib.CsaqP2PGroup
+    assert lines["layout_tier"] == f"{ctypes.sizeof(T)} {T.blocks.offset} {T.y.offset} {T.ldr.offset}"
+    assert lines["layout_gemv_ext"] == f"{ctypes.sizeof(E)} {E.x_mul.offset}"
+    assert lines["layout_p2p_group"] == f"{ctypes.sizeof(G)} {G.flags.offset} {G.err.offset}"
 
 
 def test_argument_validation_without_launch():
