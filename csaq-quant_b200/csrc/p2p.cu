@@ -111,9 +111,10 @@ __global__ void __launch_bounds__(kNormThreads)
   pdl_wait();
   const uint64_t want = exchange_signal_wait(G, spin_limit);
   __shared__ float red[32];
-  const bool vec = N % 8 == 0 && N <= kNormThreads * 8 * kNormVec && ldo % 8 == 0 && ldn % 8 == 0 &&
-                   ld_p % 8 == 0 && part_offset % 8 == 0 && reinterpret_cast<uintptr_t>(out) % 16 == 0 &&
-                   reinterpret_cast<uintptr_t>(xn) % 16 == 0 && reinterpret_cast<uintptr_t>(w) % 16 == 0;
+  bool vec = N % 8 == 0 && N <= kNormThreads * 8 * kNormVec && ldo % 8 == 0 && ldn % 8 == 0 &&
+             ld_p % 8 == 0 && part_offset % 8 == 0 && reinterpret_cast<uintptr_t>(out) % 16 == 0 &&
+             reinterpret_cast<uintptr_t>(xn) % 16 == 0 && reinterpret_cast<uintptr_t>(w) % 16 == 0;
+  for (int r = 0; r < G.n_ranks; ++r) vec = vec && reinterpret_cast<uintptr_t>(G.parts[r]) % 16 == 0;
   for (int64_t m = blockIdx.x; m < M; m += gridDim.x) {
     T* orow = out + m * ldo;
     if (vec) {
