@@ -45,6 +45,72 @@ def test_python_binding_covers_every_declared_symbol():
     assert declared <= bound, sorted(declared - bound)
 
 
+def _prototypes():
+    """name -> (return type, [parameter types]) from every prototype in include/*.h."""
+    out = {}
+    for h in glob.glob(os.path.join(REPO, "include", "*.h")):
+        src = open(h).read()
+        src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
+        src = re.sub(r"//[^\n]*", "", src)
+        for m in re.finditer(r"^\s*((?:const\s+)?[A-Za-z_0-9]+\s*\**)\s*(csaq_[a-z0-9_]+)\s*\(([^)]*)\)\s*;",
+                             src, re.M):
+            params = []
+            for p in m.group(3).split(","):
+                p = " ".join(p.split())
+                if p and p != "void":
+                    params.append(re.sub(r"\s*\b[A-Za-z_0-9]+$", "", p).replace(" *", "*"))
+            out[m.group(2)] = (" ".join(m.group(1).split()).replace(" *", "*"), params)
+    return out
+
+
+# C scalar type -> the ctypes class that passes it (same width, same signedness or float)
+_C_SCALARS = {"int": ctypes.c_int, "int64_t": ctypes.c_int64, "uint64_t": ctypes.c_uint64,
+              "uint32_t": ctypes.c_uint32, "float": ctypes.c_float}
+# pointee of a typed pointer -> the ctypes element a POINTER() argument may use
+_C_POINTEES = {"int32_t": ctypes.c_int32, "int64_t": ctypes.c_int64, "uint64_t": ctypes.c_uint64,
+               "uint32_t": ctypes.c_uint32, "uint16_t": ctypes.c_uint16, "uint8_t": ctypes.c_uint8,
+               "float": ctypes.c_float}
+
+
+def _arg_matches(c_type, ct):
+    if c_type.endswith("*"):
+        if ct in (ctypes.c_void_p, ctypes.c_char_p):
+            return True
+        if not (isinstance(ct, type) and issubclass(ct, ctypes._Pointer)):
+            return False
+        pointee = c_type[:-1].replace("const ", "").strip()
+        if pointee in _C_POINTEES:
+            return ctypes.sizeof(ct._type_) == ctypes.sizeof(_C_POINTEES[pointee])
+        return True  # a struct, checked by the layout tests
+    want = _C_SCALARS.get(c_type)
+    return want is not None and ct is want
+
+
+def test_python_signatures_match_the_header():
+    """Every ctypes binding passes what the C prototype takes: the same
+    number of arguments, pointers where it takes pointers and scalars of the
+    same width and kind (a c_int bound to an int64_t parameter would leave
+    the upper half of the register undefined)."""
+    from csaq import _lib
+    _lib.lib()
+    protos = _prototypes()
+    assert set(protos) == set(_declared_functions())
+    bad = []
+    for name, (ret, params) in sorted(protos.items()):
+        restype, argtypes = _lib._SIGNATURES[name]
+        if len(argtypes) != len(params):
+            bad.append((name, "arity", len(params), len(argtypes)))
+            continue
+        for i, (c_type, ct) in enumerate(zip(params, argtypes)):
+            if not _arg_matches(c_type, ct):
+                bad.append((name, i, c_type, ct))
+        want_ret = {"int": ctypes.c_int, "int64_t": ctypes.c_int64, "const char*": ctypes.c_char_p,
+                    "void": None}[ret]
+        if restype is not want_ret:
+            bad.append((name, "return", ret, restype))
+    assert not bad, bad
+
+
 def test_version_and_status_strings():
     from csaq import _lib
     L = _lib.lib()
