@@ -1,10 +1,13 @@
 /*
  * csaq_b200.h — C ABI of the B200 (sm_100a) quantised hot path of csaq-quant.
  *
- * Every entry point is stream-ordered (enqueues work on `stream`, a
+ * Every compute entry point is stream-ordered (enqueues work on `stream`, a
  * cudaStream_t passed as void*), never synchronises, never allocates, and
- * returns an int status (CSAQ_OK = 0, negative on error). Buffers are
- * caller-owned device pointers. Sizes are int64_t. Layouts are row-major.
+ * returns an int status (CSAQ_OK = 0, negative on error). The exception is
+ * the one-time set-up of the tensor-parallel exchange (csaq_p2p_alloc/free,
+ * csaq_ipc_open/close), which allocates and maps its buffers synchronously.
+ * Buffers are caller-owned device pointers. Sizes are int64_t. Layouts are
+ * row-major.
  *
  * Packed-code layout (identical to csaq-quant's storage):
  *   bits 8: one byte per code;   bits 4: byte j = col 2j (low nibble) | col 2j+1 (high);
